@@ -1,0 +1,399 @@
+"""Whole-encoder images/s on B200s, with per-kernel roofline and a CPU baseline.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Workload: the Qwen3.5-0.8B vision encoder at 512x512
+(1024 tokens, grid 32x32), fp16 weights and activations, a global batch of 64
+seeded synthetic images sharded by image over N GPUs (one process per GPU,
+launched by torchrun for N > 1); the embedding all-gather is the only
+collective. One step = the whole encoder over the whole batch.
+
+  value    images/s of the whole job, device-timed with CUDA events on the
+           session stream, inputs resident in HBM, max over ranks.
+  e2e      the same through the public API (Session.run): per step, the
+           host->device copy of the step's images from pinned memory, the
+           plan, the device->host copy of the embeddings (and the all-gather
+           for N > 1).
+  roofline the dominant kernel (largest share of one eager, op-by-op timed
+           pass): algorithmic FLOPs or bytes per launch / its mean CUDA-event
+           duration, against MEASURED_PEAKS.json.
+  cpu_baseline  the numpy oracle port (a restatement of hexlib's reference
+           executor) on this host's cores, one image (rank 0, N = 1 only).
+
+`--impl reference` times that CPU port alone on the same metric and prints
+its line (rank 0; other ranks exit at once).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "encoder images/s"
+UNIT = "images/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--image-size", type=int, default=512)
+    ap.add_argument("--batch", type=int, default=64, help="global batch (images)")
+    ap.add_argument("--no-attention-fusion", action="store_true")
+    ap.add_argument("--no-residual-fusion", action="store_true")
+    return ap.parse_args()
+
+
+def peaks() -> dict:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            m = json.load(f)
+        return {"hbm": m["hbm_gbs"], "tc": m["bf16_tflops"],
+                "tc_sustained": m.get("bf16_tflops_sustained", m["bf16_tflops"]),
+                "src": "measured"}
+    except Exception:  # noqa: BLE001
+        return {"hbm": 6650.0, "tc": 1590.0, "tc_sustained": 1400.0, "src": "fallback"}
+
+
+# ---- CPU baseline ----------------------------------------------------------------
+
+def cpu_port_time(cfg, n_images: int, warm: bool = True) -> tuple[float, int, str]:
+    """Seconds per image of the oracle port (hexlib's reference executor,
+    restated) over `n_images` images, on all BLAS threads of this host."""
+    import numpy as np  # noqa: F401
+
+    from hexlib_b200 import feeds as F
+    from hexlib_b200 import graph as G
+    from oracle import executor
+    g = G.build_vision_encoder(cfg)
+    ep = G.compile_for_cuda(g)
+    w = F.weights(cfg, 0, g)
+    imgs = F.images(cfg, n_images, 1)
+    if warm:  # page in numpy/BLAS on a small model
+        small = G.qwen35_at(64)
+        gs = G.build_vision_encoder(small)
+        executor.run(G.compile_for_cuda(gs), dict(F.weights(small, 0, gs),
+                                                  image=F.images(small, 1, 1)[0]))
+    t0 = time.perf_counter()
+    for i in range(n_images):
+        executor.run(ep, dict(w, image=imgs[i]))
+    dt = (time.perf_counter() - t0) / n_images
+    threads = os.cpu_count() or 1
+    try:
+        import threadpoolctl
+        info = threadpoolctl.threadpool_info()
+        threads = max([i.get("num_threads", 1) for i in info] + [1])
+    except Exception:  # noqa: BLE001
+        pass
+    return dt, threads, f"{n_images} image(s) at {cfg.image_size}x{cfg.image_size}"
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from hexlib_b200 import graph as G
+    cfg = G.qwen35_at(args.image_size)
+    # Each image is ~20-30 s of CPU at 512^2: time at most 3 so the arm ends
+    # within a few minutes whatever --steps asks for.
+    n = max(1, min(args.steps, 3))
+    dt, threads, sample = cpu_port_time(cfg, n, warm=args.warmup > 0)
+    v = 1.0 / dt
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": n, "warmup": min(args.warmup, 1),
+        "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "fp16 storage, fp32/fp64 compute",
+        "data": "synthetic (seeded images and N(0,0.02) weights)",
+        "config": {"workload": f"qwen35 vision encoder {cfg.image_size}x{cfg.image_size}, "
+                               f"global batch {args.batch}, fp16", "image_size": cfg.image_size,
+                   "global_batch": args.batch, "seq_len": cfg.num_tokens,
+                   "parallelism": "cpu, one process"},
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": sample + ", numpy restatement of hexlib's reference "
+                                            "plan executor (oracle/executor.py)"},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---- clocks --------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.index), "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:  # noqa: BLE001
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:  # noqa: BLE001
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(nm)
+        busy = [x for x in sm if mx and x > 0.3 * mx] or sm
+        return {"sm_mhz": statistics.median(busy) if busy else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---- the B200 arm ------------------------------------------------------------------------
+
+def op_work(plan, op_index: int, n_images: int) -> tuple[str, float, str]:
+    """(bound, algorithmic work per launch, unit) for one op of the plan."""
+    import numpy as np  # noqa: F401
+    from hexlib_b200 import wire
+    blob = plan.blob
+    hdr = wire.HDR.unpack_from(blob)
+    f = wire.OP.unpack_from(blob, hdr[8] + op_index * wire.OP_SIZE)
+    srcs = [s for s in f[18:24] if s != 0xFFFF]
+    dsts = [d for d in f[24:28] if d != 0xFFFF]
+    names = {v: k for k, v in plan.index.items()}
+    P = plan.placements
+    vname = plan.kinds[op_index]
+
+    def nb(n):
+        p = P[names[n]]
+        return p.nbytes * (n_images if p.buffer == 1 else 1)
+
+    if vname in ("matmul_epilogue", "matmul_epilogue_residual"):
+        a, w = P[names[srcs[0]]], P[names[srcs[1]]]
+        M = a.shape[0] * n_images
+        K, N = w.shape
+        return "tensor", 2.0 * M * N * K, "FLOP"
+    if vname == "matmul":
+        a, b = P[names[srcs[0]]], P[names[srcs[1]]]
+        Bn, M, K = a.shape
+        return "tensor", 2.0 * Bn * n_images * M * b.shape[2] * K, "FLOP"
+    if vname == "attention":
+        q = P[names[srcs[0]]]
+        Bn, T, D = q.shape
+        return "tensor", 4.0 * Bn * n_images * T * T * D, "FLOP"
+    return "hbm", float(sum(nb(s) for s in srcs) + sum(nb(d) for d in dsts)), "B"
+
+
+def run_b200(args) -> None:
+    import numpy as np
+    import torch
+
+    from hexlib_b200 import dist as D
+    from hexlib_b200 import feeds as F
+    from hexlib_b200 import graph as G
+    from hexlib_b200 import wholeplan
+    from hexlib_b200.session import MODE_EAGER, Session, attention_available
+
+    rank, local, world = D.env_rank()
+    torch.cuda.set_device(local)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+        pg = dist
+
+    cfg = G.qwen35_at(args.image_size)
+    g = G.build_vision_encoder(cfg)
+    use_att = (not args.no_attention_fusion) and attention_available()
+    ep = G.compile_for_cuda(g, attention=use_att, residual=not args.no_residual_fusion)
+    w = F.weights(cfg, 0, g)
+    plan = wholeplan.build_cuda_plan(ep, w, alias=True)
+    sh = D.shard(args.batch, rank, world)
+    n = sh.count
+    imgs = F.images(cfg, n, seed=1 + sh.start)
+    host_in = torch.from_numpy(imgs).pin_memory()
+    out_p = plan.placements[plan.outputs[0]]
+    host_out = torch.empty((n,) + tuple(out_p.shape), dtype=torch.float16).pin_memory()
+
+    s = Session(local)
+    s.load(plan, max_images=n)
+    s.write_input(plan.inputs[0], host_in, n)
+    stream = torch.cuda.ExternalStream(s.stream(), device=torch.device("cuda", local))
+    emb = s.device_view(plan.outputs[0], n)
+
+    def step_device():
+        s.invoke(n, sync=False)
+        if pg is not None:
+            with torch.cuda.stream(stream):
+                D.gather_embeddings(emb)
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+        torch.cuda.synchronize()
+        s.sync()
+
+    warm = max(args.warmup, 3)
+    for _ in range(warm):
+        step_device()
+    s.sync()
+
+    # ---- device-timed, inputs resident ----------------------------------------------
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step_device()
+    e1.record(stream)
+    s.sync()
+    e1.synchronize()
+    ms = e0.elapsed_time(e1)
+    clk = clocks.stop()
+    t = torch.tensor([ms], device="cuda")
+    if pg is not None:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = args.batch * args.steps / (ms_max / 1e3)
+
+    # ---- end to end through Session.run (pinned host buffers) ---------------------
+    barrier()
+    e2 = torch.cuda.Event(enable_timing=True)
+    e3 = torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    for _ in range(args.steps):
+        s.run(host_in, out=host_out.numpy())
+        if pg is not None:
+            with torch.cuda.stream(stream):
+                D.gather_embeddings(emb)
+    e3.record(stream)
+    e3.synchronize()
+    ms_e2e = e2.elapsed_time(e3)
+    t = torch.tensor([ms_e2e], device="cuda")
+    if pg is not None:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    e2e = args.batch * args.steps / (float(t.item()) / 1e3)
+
+    # ---- roofline of the dominant kernel (one eager, op-by-op timed pass) -----------
+    rsp = s.invoke(n, mode=MODE_EAGER)
+    per_op = [r.cycles for r in rsp.results]
+    groups: dict[tuple, list[int]] = {}
+    for i, ns in enumerate(per_op):
+        bound, work, unit = op_work(plan, i, n)
+        groups.setdefault((plan.kinds[i], bound, work, unit), []).append(ns)
+    total_ns = sum(per_op)
+    table = sorted(((sum(v), k, v) for k, v in groups.items()), reverse=True)
+    pk = peaks()
+    dom_ns, (dname, dbound, dwork, dunit), dlist = table[0]
+    mean_s = (dom_ns / len(dlist)) / 1e9
+    if dbound == "tensor":
+        achieved = dwork / mean_s / 1e12
+        peak, punit = pk["tc_sustained"], "TFLOP/s"
+    else:
+        achieved = dwork / mean_s / 1e9
+        peak, punit = pk["hbm"], "GB/s"
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            tr = json.load(f)
+        traffic = tr.get(dname)
+    except Exception:  # noqa: BLE001
+        pass
+
+    kernels = []
+    for tot, (kname, bound, work, unit), lst in table:
+        m = tot / len(lst) / 1e9
+        kernels.append({"kernel": kname, "launches": len(lst), "share": tot / total_ns,
+                        "mean_us": m * 1e6,
+                        "achieved": (work / m / 1e12) if bound == "tensor" else (work / m / 1e9),
+                        "unit": "TFLOP/s" if bound == "tensor" else "GB/s"})
+
+    cpu = None
+    if world == 1 and rank == 0 and os.environ.get("HEXLIB_B200_BENCH_NO_CPU") != "1":
+        dt, threads, sample = cpu_port_time(cfg, 1)
+        cpu = {"value": 1.0 / dt, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": sample + " through the numpy restatement of hexlib's reference "
+                                  "plan executor (oracle/executor.py)"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": warm, "ms_per_step": ms_max / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "fp16", "data": "synthetic (seeded images, N(0,0.02) fp16 weights)",
+            "config": {
+                "workload": f"qwen35 vision encoder {cfg.image_size}x{cfg.image_size}, "
+                            f"global batch {args.batch}, sharded by image",
+                "image_size": cfg.image_size, "global_batch": args.batch,
+                "seq_len": cfg.num_tokens, "parallelism": f"image-sharded x{world}",
+                "plan_ops": plan.n_ops, "fusions": {"attention": use_att,
+                                                   "residual": not args.no_residual_fusion},
+                "l2": "inputs larger than L2: each step reads 201 MB of weights and "
+                      f"{n * 6.29:.0f} MB of images per GPU",
+            },
+            "e2e": {"value": e2e, "unit": UNIT,
+                    "h2d_bytes_per_step": int(host_in.numel() * 4),
+                    "d2h_bytes_per_step": int(host_out.numel() * 2)},
+            "gpu_launches": plan.n_ops * args.steps,
+            "roofline": {"kernel": dname, "bound": dbound, "achieved": achieved,
+                         "peak": peak, "unit": punit, "frac": achieved / peak,
+                         "peak_source": f"{pk['src']} "
+                                        f"({'sustained bf16' if dbound == 'tensor' else 'hbm copy'})",
+                         "traffic": traffic, "share": dom_ns / total_ns},
+            "kernels": kernels[:8],
+            "clocks": clk,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    s.close()
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

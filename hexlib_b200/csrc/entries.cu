@@ -1,0 +1,223 @@
+// entries.cu -- the kernel_api.h-shaped C entry points of libhexlib_b200.
+//
+// One function per kernels/<k>/kernel_api.h signature, with a trailing stream
+// and an int status. They validate their scalar arguments, then call the same
+// launcher the batch dispatcher uses, with one image.
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "../../include/hexlib_b200.h"
+#include "hb_kernels.h"
+
+namespace hb {
+
+int memory_kernels_init();
+int gemm_kernels_init();
+int attention_kernels_init();
+
+namespace {
+std::once_flag g_init_once;
+int g_init_status = HEXLIB_B200_ERR_INTERNAL;
+int* g_err_dev = nullptr;
+}  // namespace
+
+int kernels_init() {
+  std::call_once(g_init_once, [] {
+    int rc = memory_kernels_init();
+    if (rc == HEXLIB_B200_OK) rc = gemm_kernels_init();
+    if (rc == HEXLIB_B200_OK) rc = attention_kernels_init();
+    int* host = nullptr;
+    if (rc == HEXLIB_B200_OK &&
+        cudaHostAlloc(reinterpret_cast<void**>(&host), sizeof(int),
+                      cudaHostAllocMapped) == cudaSuccess) {
+      *host = 0;
+      if (cudaHostGetDevicePointer(reinterpret_cast<void**>(&g_err_dev), host,
+                                   0) != cudaSuccess)
+        rc = HEXLIB_B200_ERR_CUDA;
+    } else if (rc == HEXLIB_B200_OK) {
+      rc = HEXLIB_B200_ERR_CUDA;
+    }
+    if (rc != HEXLIB_B200_OK) cudaGetLastError();
+    g_init_status = rc;
+  });
+  return g_init_status;
+}
+
+int* default_error_word() { return g_err_dev; }
+
+}  // namespace hb
+
+using hb::kernels_init;
+
+#define HB_ENTRY_INIT()                              \
+  do {                                               \
+    const int _rc = kernels_init();                  \
+    if (_rc != HEXLIB_B200_OK) return _rc;           \
+  } while (0)
+
+static inline cudaStream_t as_stream(void* s) {
+  return reinterpret_cast<cudaStream_t>(s);
+}
+
+extern "C" {
+
+int hexlib_b200_add_fp16(const void* a, const void* b, void* y, int n,
+                         void* stream) {
+  HB_ENTRY_INIT();
+  if (n < 0 || (n > 0 && (!a || !b || !y))) return HEXLIB_B200_ERR_INVAL_PARAMS;
+  return hb::launch_add_f16(a, b, y, n, n > 0 ? n : 1, as_stream(stream));
+}
+
+int hexlib_b200_add_fp16_f32(const void* a, const float* b, void* y, int n,
+                             void* stream) {
+  HB_ENTRY_INIT();
+  if (n < 0 || (n > 0 && (!a || !b || !y))) return HEXLIB_B200_ERR_INVAL_PARAMS;
+  return hb::launch_add_f16_f32(a, b, y, n, n > 0 ? n : 1, as_stream(stream));
+}
+
+int hexlib_b200_cast_f32_f16(const float* x, void* y, int n, void* stream) {
+  HB_ENTRY_INIT();
+  if (n < 0 || (n > 0 && (!x || !y))) return HEXLIB_B200_ERR_INVAL_PARAMS;
+  return hb::launch_cast_f32_f16(x, y, n, as_stream(stream));
+}
+
+int hexlib_b200_scale_fp16(const void* x, void* y, int n, float factor,
+                           void* stream) {
+  HB_ENTRY_INIT();
+  if (n < 0 || (n > 0 && (!x || !y))) return HEXLIB_B200_ERR_INVAL_PARAMS;
+  return hb::launch_scale_f16(x, y, n, factor, as_stream(stream));
+}
+
+int hexlib_b200_layernorm_fp16(const void* x, const float* w, const float* b,
+                               void* y, int R, int C, float eps,
+                               void* stream) {
+  HB_ENTRY_INIT();
+  if (R < 0 || C <= 0 || (R > 0 && (!x || !w || !b || !y)))
+    return HEXLIB_B200_ERR_INVAL_PARAMS;
+  return hb::launch_layernorm_f16(x, w, b, y, R, C, eps, as_stream(stream));
+}
+
+int hexlib_b200_rmsnorm_fp16(const void* x, const void* w, void* y, int R,
+                             int C, float eps, void* stream) {
+  HB_ENTRY_INIT();
+  if (R < 0 || C <= 0 || (R > 0 && (!x || !w || !y)))
+    return HEXLIB_B200_ERR_INVAL_PARAMS;
+  return hb::launch_rmsnorm_f16(x, w, y, R, C, eps, as_stream(stream));
+}
+
+int hexlib_b200_softmax_fp16(const void* x, void* y, int R, int C,
+                             void* stream) {
+  HB_ENTRY_INIT();
+  if (R < 0 || C <= 0 || (R > 0 && (!x || !y)))
+    return HEXLIB_B200_ERR_INVAL_PARAMS;
+  return hb::launch_softmax_f16(x, y, R, C, as_stream(stream));
+}
+
+int hexlib_b200_rope_2d_fp16(const void* x, const float* costab,
+                             const float* sintab, void* y, int T, int H, int D,
+                             void* stream) {
+  HB_ENTRY_INIT();
+  if (T < 0 || H <= 0 || D <= 0 || (D & 1) ||
+      (T > 0 && (!x || !costab || !sintab || !y)))
+    return HEXLIB_B200_ERR_INVAL_PARAMS;
+  if (T == 0) return HEXLIB_B200_OK;
+  return hb::launch_rope_f16(x, costab, sintab, y, T, H, D, T,
+                             as_stream(stream));
+}
+
+int hexlib_b200_transpose_th_fp16(const void* x, void* y, int T, int H, int D,
+                                  void* stream) {
+  HB_ENTRY_INIT();
+  if (T <= 0 || H <= 0 || D <= 0 || !x || !y)
+    return HEXLIB_B200_ERR_INVAL_PARAMS;
+  return hb::launch_transpose_th_f16(x, y, 1, T, H, D, as_stream(stream));
+}
+
+int hexlib_b200_transpose_hd_fp16(const void* x, void* y, int B, int T, int D,
+                                  void* stream) {
+  HB_ENTRY_INIT();
+  if (B < 0 || T <= 0 || D <= 0 || (B > 0 && (!x || !y)))
+    return HEXLIB_B200_ERR_INVAL_PARAMS;
+  return hb::launch_transpose_hd_f16(x, y, B, T, D, as_stream(stream));
+}
+
+int hexlib_b200_patchify_fp32(const float* img, float* out, int C, int T,
+                              int H, int W, int patch, int merge, int grid_h,
+                              int grid_w, void* stream) {
+  HB_ENTRY_INIT();
+  if (!img || !out) return HEXLIB_B200_ERR_INVAL_PARAMS;
+  return hb::launch_patchify_f32(img, out, 1, C, T, H, W, patch, merge, grid_h,
+                                 grid_w, as_stream(stream));
+}
+
+int hexlib_b200_matmul_fp16(const void* A, const void* B, void* C, int Bn,
+                            int M, int K, int N, void* stream) {
+  HB_ENTRY_INIT();
+  if (Bn < 0 || M < 0 || K <= 0 || N <= 0) return HEXLIB_B200_ERR_INVAL_PARAMS;
+  hb::GemmDesc g{};
+  g.A = A;
+  g.B = B;
+  g.out = C;
+  g.batch = Bn;
+  g.M = M;
+  g.K = K;
+  g.N = N;
+  g.b_shared = false;
+  g.act = 0;
+  return hb::launch_gemm(g, hb::default_error_word(), as_stream(stream));
+}
+
+int hexlib_b200_matmul_epilogue_fp16(const void* a, const void* w,
+                                     const float* bias, void* out, int M,
+                                     int K, int N, int act, void* stream) {
+  HB_ENTRY_INIT();
+  if (M < 0 || K <= 0 || N <= 0 || act < 0 || act > 2 || !bias)
+    return HEXLIB_B200_ERR_INVAL_PARAMS;
+  hb::GemmDesc g{};
+  g.A = a;
+  g.B = w;
+  g.bias = bias;
+  g.out = out;
+  g.batch = 1;
+  g.M = M;
+  g.K = K;
+  g.N = N;
+  g.b_shared = true;
+  g.act = act;
+  return hb::launch_gemm(g, hb::default_error_word(), as_stream(stream));
+}
+
+int hexlib_b200_matmul_epilogue_residual_fp16(const void* a, const void* w,
+                                              const float* bias, const void* r,
+                                              void* out, int M, int K, int N,
+                                              int act, void* stream) {
+  HB_ENTRY_INIT();
+  if (M < 0 || K <= 0 || N <= 0 || act < 0 || act > 2 || !bias || !r)
+    return HEXLIB_B200_ERR_INVAL_PARAMS;
+  hb::GemmDesc g{};
+  g.A = a;
+  g.B = w;
+  g.bias = bias;
+  g.resid = r;
+  g.out = out;
+  g.batch = 1;
+  g.M = M;
+  g.K = K;
+  g.N = N;
+  g.b_shared = true;
+  g.act = act;
+  return hb::launch_gemm(g, hb::default_error_word(), as_stream(stream));
+}
+
+int hexlib_b200_attention_fp16(const void* q, const void* k, const void* v,
+                               void* ctx, int Bn, int T, int D, float scale,
+                               void* stream) {
+  HB_ENTRY_INIT();
+  if (Bn < 0 || T <= 0 || D <= 0 || (Bn > 0 && (!q || !k || !v || !ctx)))
+    return HEXLIB_B200_ERR_INVAL_PARAMS;
+  return hb::launch_attention(q, k, v, ctx, Bn, T, D, scale,
+                              hb::default_error_word(), as_stream(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,83 @@
+// hb_kernels.h -- host-side launchers for every kernel in libhexlib_b200.
+//
+// Each launcher enqueues its kernel(s) on `stream` and returns a status
+// (HEXLIB_B200_OK, or HEXLIB_B200_ERR_INVAL_PARAMS for arguments it cannot
+// serve); none allocates memory or synchronises, so every one of them can be
+// recorded into a CUDA graph. The public kernel_api.h-shaped entry points and
+// the batch dispatcher both call these, with the batch dimension the
+// dispatcher folds in (images per launch) passed explicitly.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/hexlib_b200.h"
+
+namespace hb {
+
+// Elementwise. `nb` is the right operand's element count: it is broadcast
+// with period nb (nb == n for a plain add; nb < n when a per-image tensor is
+// added to one shared by every image).
+int launch_add_f16(const void* a, const void* b, void* y, int64_t n,
+                   int64_t nb, cudaStream_t s);
+int launch_add_f16_f32(const void* a, const float* b, void* y, int64_t n,
+                       int64_t nb, cudaStream_t s);
+int launch_cast_f32_f16(const float* x, void* y, int64_t n, cudaStream_t s);
+int launch_scale_f16(const void* x, void* y, int64_t n, float factor,
+                     cudaStream_t s);
+int launch_copy(const void* x, void* y, int64_t nbytes, cudaStream_t s);
+
+// Row-wise.
+int launch_layernorm_f16(const void* x, const float* w, const float* b,
+                         void* y, int64_t R, int C, float eps, cudaStream_t s);
+int launch_rmsnorm_f16(const void* x, const void* w, void* y, int64_t R, int C,
+                       float eps, cudaStream_t s);
+int launch_softmax_f16(const void* x, void* y, int64_t R, int C,
+                       cudaStream_t s);
+// rows = tokens over every image; the cos/sin tables have `table_rows` rows
+// and token r uses table row r % table_rows.
+int launch_rope_f16(const void* x, const float* cos_t, const float* sin_t,
+                    void* y, int64_t rows, int H, int D, int64_t table_rows,
+                    cudaStream_t s);
+
+// Layout moves. `nimg` independent [T,H,D] -> [H,T,D] permutes.
+int launch_transpose_th_f16(const void* x, void* y, int64_t nimg, int T, int H,
+                            int D, cudaStream_t s);
+// [B,T,D] -> [B,D,T].
+int launch_transpose_hd_f16(const void* x, void* y, int64_t B, int T, int D,
+                            cudaStream_t s);
+int launch_patchify_f32(const float* img, float* out, int64_t nimg, int C,
+                        int T, int H, int W, int patch, int merge, int grid_h,
+                        int grid_w, cudaStream_t s);
+
+// Tensor-core GEMMs (tcgen05), with a CUDA-core fallback for shapes the TMA
+// path cannot describe (K or N not a multiple of 8, misaligned pointers).
+//   out[b] = act(A[b] @ W[b or shared] + bias) (+ resid[b])
+struct GemmDesc {
+  const void* A;       // [batch, M, K] fp16 row-major
+  const void* B;       // [batch or 1, K, N] fp16 row-major (MN-major operand)
+  const float* bias;   // [N] or nullptr
+  const void* resid;   // [batch, M, N] fp16 or nullptr
+  void* out;           // [batch, M, N] fp16
+  int64_t batch;       // independent products
+  int64_t M;
+  int K, N;
+  bool b_shared;       // B has one copy used by every batch entry
+  int act;             // 0 none, 1 gelu_tanh, 2 gelu_erf
+};
+int launch_gemm(const GemmDesc& g, int* err, cudaStream_t s);
+
+// Fused attention: q, k, v, ctx are [Bn, T, D] fp16.
+int launch_attention(const void* q, const void* k, const void* v, void* ctx,
+                     int64_t Bn, int T, int D, float scale, int* err,
+                     cudaStream_t s);
+
+// One-time per-process setup of kernel attributes (dynamic shared memory
+// limits); safe to call repeatedly. Returns a status.
+int kernels_init();
+
+// The session-independent device error word that kernels launched through
+// the public per-kernel entry points report bounded-wait timeouts in.
+int* default_error_word();
+
+}  // namespace hb

@@ -1,0 +1,454 @@
+// k_gemm.cu -- fp16 GEMM on the sm_100a tensor cores (tcgen05 + TMEM + TMA),
+// with the matmul_epilogue epilogue fused: out = act(A @ W + bias) (+ resid).
+//
+// Serves both wire kernels that contract over a dense operand:
+//   matmul_epilogue (kernels/matmul_epilogue_fp16/kernel_api.h:188-190, with an
+//     fp16 [K, N] weight): A [M, K] per image, W [K, N] shared, bias fp32 [N];
+//     the images fold into M, so one launch covers B*T rows.
+//   matmul (kernels/matmul_fp16/kernel_api.h:77-78): batched A [Bn, M, K] @
+//     B [Bn, K, N], no bias, no activation (attention QK^T and PV).
+// Accumulation is fp32 in tensor memory and the output is rounded to fp16
+// exactly once, after the bias and the activation (fused.py:44-53).
+//
+// STRUCTURE. A persistent kernel, one CTA per SM, tiles of 128 x BN, K in
+// blocks of 64 (one 128-byte swizzle row of fp16):
+//   warp 0      TMA producer: A tile [128 x 64] and BN/64 W tiles [64 x 64]
+//               per stage, into a STAGES-deep ring of shared-memory buffers;
+//   warp 1      allocates tensor memory, and one lane issues tcgen05.mma
+//               (M=128, N=BN, K=16) four times per stage into one of two
+//               accumulators, then commits to free the stage;
+//   warps 2-9   epilogue: tcgen05.ld the finished accumulator (two warps per
+//               32-lane quarter, each taking half of the columns), add bias,
+//               apply GELU, round, store; then release the accumulator so the
+//               MMA of the tile after next can reuse it.
+// Two accumulators let the epilogue of tile i overlap the MMAs of tile i+1.
+//
+// A is K-major (row-major [M, K]); W is MN-major (row-major [K, N]) and is
+// consumed in place through the descriptor's MN-major mode, so no weight is
+// ever transposed.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <mutex>
+
+#include "hb_device.cuh"
+#include "hb_kernels.h"
+#include "hb_tma.h"
+
+namespace hb {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int kEpiWarps = 8;
+constexpr int kGemmThreads = 64 + kEpiWarps * 32;  // 320
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int STAGES = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+  static constexpr int A_BYTES = BM * BK * 2;   // 16 KiB
+  static constexpr int B_BYTES = BN * BK * 2;   // BN/64 boxes of 8 KiB
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN;      // two fp32 accumulators
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+};
+
+struct GemmParams {
+  int64_t M;        // rows per batch entry
+  int K, N;
+  int64_t batch;
+  int tiles_m, tiles_n;
+  int64_t total_tiles;
+  int num_kb;
+  int b_shared;
+  int act;
+  const float* bias;
+  const __half* resid;
+  __half* out;
+  int* err;
+};
+
+template <int BN>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_f16_tc(const __grid_constant__ CUtensorMap tmA,
+                const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
+  using Cfg = GemmCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + Cfg::STAGES * Cfg::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + Cfg::STAGES * Cfg::B_BYTES);
+  uint64_t* empty = full + Cfg::STAGES;
+  uint64_t* tfull = empty + Cfg::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Cfg::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], kEpiWarps);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int64_t tiles_per_batch = (int64_t)p.tiles_m * p.tiles_n;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int64_t t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
+        const int64_t b = t / tiles_per_batch;
+        const int64_t r = t - b * tiles_per_batch;
+        const int mb = (int)(r / p.tiles_n);
+        const int nb = (int)(r % p.tiles_n);
+        const int bz = p.b_shared ? 0 : (int)b;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err))
+            goto done;
+          mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+          tma_load_3d(&tmA, &full[stage], sA + stage * Cfg::A_BYTES, kb * BK,
+                      mb * BM, (int)b);
+#pragma unroll
+          for (int j = 0; j < BN / 64; ++j)
+            tma_load_3d(&tmB, &full[stage],
+                        sB + stage * Cfg::B_BYTES + j * (BK * 128),
+                        nb * BN + j * 64, kb * BK, bz);
+          if (++stage == Cfg::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(BM, BN, false, true);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int64_t t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, p.err))
+          goto done;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.err)) goto done;
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * Cfg::A_BYTES);
+          const uint32_t b0 = smem_u32(sB + stage * Cfg::B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            // A: advance 16 fp16 (32 bytes) along the swizzled row.
+            const uint64_t ad = sdesc_sw128(a0 + kk * 32, 16, 1024);
+            // W: advance 16 k-rows = two 1024-byte atoms; 64-wide N boxes
+            // are BK*128 bytes apart.
+            const uint64_t bd = sdesc_sw128(b0 + kk * 2048, BK * 128, 1024);
+            umma_f16(d_tmem, ad, bd, idesc, (kb | kk) ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == Cfg::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        umma_commit(&tfull[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+    }
+  } else {
+    const int ew = warp - 2;
+    const int quarter = warp & 3;  // TMEM lanes this warp may access
+    const int colhalf = ew >> 2;
+    constexpr int kChunks = BN / 32;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int64_t t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
+      const int64_t b = t / tiles_per_batch;
+      const int64_t r = t - b * tiles_per_batch;
+      const int mb = (int)(r / p.tiles_n);
+      const int nb = (int)(r % p.tiles_n);
+      // Every lane waits; the warp proceeds only if all of them saw the
+      // phase complete, because tcgen05.ld below is warp-collective.
+      const bool ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, p.err);
+      if (!__all_sync(0xffffffffu, ok)) goto done;
+      tc_fence_after();
+      const int64_t row = (int64_t)mb * BM + quarter * 32 + lane;
+      const bool row_ok = row < p.M;
+      const uint32_t trow =
+          tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+      __half* orow = p.out + (b * p.M + row) * (int64_t)p.N;
+      const __half* rrow =
+          p.resid ? p.resid + (b * p.M + row) * (int64_t)p.N : nullptr;
+#pragma unroll 1
+      for (int c = colhalf * (kChunks / 2); c < (colhalf + 1) * (kChunks / 2);
+           ++c) {
+        uint32_t rg[32];
+        tmem_ld_32x32b_x32(trow + c * 32, rg);
+        tmem_ld_wait();
+        const int n0 = nb * BN + c * 32;
+        if (row_ok && n0 < p.N) {
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(rg[j]);
+          if (p.bias) {
+            const float4* bp = reinterpret_cast<const float4*>(p.bias + n0);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              if (n0 + 4 * j < p.N) {
+                const float4 bb = __ldg(bp + j);
+                v[4 * j] += bb.x;
+                v[4 * j + 1] += bb.y;
+                v[4 * j + 2] += bb.z;
+                v[4 * j + 3] += bb.w;
+              }
+            }
+          }
+          if (p.act == 1) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = gelu_tanh_f(v[j]);
+          } else if (p.act == 2) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = gelu_erf_f(v[j]);
+          }
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            if (n0 + 8 * g >= p.N) break;
+            uint4 o;
+            uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+            if (rrow) {
+              const uint4 rv = __ldg(reinterpret_cast<const uint4*>(rrow + n0) + g);
+              const __half2* rh = reinterpret_cast<const __half2*>(&rv);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                // The matmul result is an fp16 tensor in the unfused plan:
+                // round it, then add the residual in fp32 and round again.
+                const __half2 mm = __floats2half2_rn(v[8 * g + 2 * q],
+                                                     v[8 * g + 2 * q + 1]);
+                const float2 fm = __half22float2(mm);
+                const float2 fr = __half22float2(rh[q]);
+                ow[q] = pack_half2(fr.x + fm.x, fr.y + fm.y);
+              }
+            } else {
+#pragma unroll
+              for (int q = 0; q < 4; ++q)
+                ow[q] = pack_half2(v[8 * g + 2 * q], v[8 * g + 2 * q + 1]);
+            }
+            reinterpret_cast<uint4*>(orow + n0)[g] = o;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+done:
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+// CUDA-core fallback for shapes the TMA path cannot describe. 64x64 output
+// tiles, K in steps of 16 through shared memory, fp32 accumulate.
+__global__ void gemm_f16_simt(const __half* __restrict__ A,
+                              const __half* __restrict__ B,
+                              const float* __restrict__ bias,
+                              const __half* __restrict__ resid,
+                              __half* __restrict__ out, int64_t M, int K,
+                              int N, int64_t batch, int b_shared, int act) {
+  __shared__ float sa[16][65];
+  __shared__ float sb[16][65];
+  const int tiles_m = (int)((M + 63) / 64), tiles_n = (N + 63) / 64;
+  const int64_t total = batch * tiles_m * (int64_t)tiles_n;
+  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;  // 16 x 16 threads
+  for (int64_t t = blockIdx.x; t < total; t += gridDim.x) {
+    const int64_t b = t / ((int64_t)tiles_m * tiles_n);
+    const int rem = (int)(t - b * tiles_m * (int64_t)tiles_n);
+    const int64_t m0 = (int64_t)(rem / tiles_n) * 64;
+    const int n0 = (rem % tiles_n) * 64;
+    const __half* Ab = A + b * M * K;
+    const __half* Bb = B + (b_shared ? 0 : b) * (int64_t)K * N;
+    float acc[4][4] = {};
+    for (int k0 = 0; k0 < K; k0 += 16) {
+      for (int e = threadIdx.x; e < 16 * 64; e += 256) {
+        const int kk = e / 64, mm = e % 64;
+        const int64_t gm = m0 + mm;
+        const int gk = k0 + kk;
+        sa[kk][mm] = (gm < M && gk < K) ? __half2float(Ab[gm * K + gk]) : 0.f;
+        const int gn = n0 + mm;
+        sb[kk][mm] = (gk < K && gn < N) ? __half2float(Bb[(int64_t)gk * N + gn]) : 0.f;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int kk = 0; kk < 16; ++kk)
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            acc[i][j] += sa[kk][ty * 4 + i] * sb[kk][tx * 4 + j];
+      __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t gm = m0 + ty * 4 + i;
+      if (gm >= M) continue;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int gn = n0 + tx * 4 + j;
+        if (gn >= N) continue;
+        float v = acc[i][j] + (bias ? bias[gn] : 0.f);
+        if (act == 1) v = gelu_tanh_f(v);
+        if (act == 2) v = gelu_erf_f(v);
+        const int64_t o = (b * M + gm) * N + gn;
+        if (resid)
+          v = __half2float(resid[o]) + __half2float(__float2half_rn(v));
+        out[o] = __float2half_rn(v);
+      }
+    }
+  }
+}
+
+int g_sm_count = 0;
+
+int sm_count() {
+  if (g_sm_count == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_sm_count, cudaDevAttrMultiProcessorCount, dev);
+    if (g_sm_count <= 0) g_sm_count = 148;
+  }
+  return g_sm_count;
+}
+
+template <int BN>
+int launch_tc(const GemmDesc& g, int* err, cudaStream_t s) {
+  using Cfg = GemmCfg<BN>;
+  CUtensorMap ta, tb;
+  // A: dims (K, M, batch); box (64, 128, 1).
+  if (!make_tmap_3d_f16(&ta, g.A, (uint64_t)g.K, (uint64_t)g.M,
+                        (uint64_t)g.batch, BK, BM))
+    return -1;
+  // W: dims (N, K, batch or 1); box (64, 64, 1).
+  if (!make_tmap_3d_f16(&tb, g.B, (uint64_t)g.N, (uint64_t)g.K,
+                        (uint64_t)(g.b_shared ? 1 : g.batch), 64, BK))
+    return -1;
+  GemmParams p;
+  p.M = g.M;
+  p.K = g.K;
+  p.N = g.N;
+  p.batch = g.batch;
+  p.tiles_m = (int)((g.M + BM - 1) / BM);
+  p.tiles_n = (g.N + BN - 1) / BN;
+  p.total_tiles = g.batch * (int64_t)p.tiles_m * p.tiles_n;
+  p.num_kb = (g.K + BK - 1) / BK;
+  p.b_shared = g.b_shared ? 1 : 0;
+  p.act = g.act;
+  p.bias = g.bias;
+  p.resid = reinterpret_cast<const __half*>(g.resid);
+  p.out = reinterpret_cast<__half*>(g.out);
+  p.err = err;
+  const int64_t grid64 =
+      p.total_tiles < sm_count() ? p.total_tiles : (int64_t)sm_count();
+  gemm_f16_tc<BN><<<(int)grid64, kGemmThreads, Cfg::SMEM_BYTES, s>>>(ta, tb,
+                                                                      p);
+  if (cudaPeekAtLastError() != cudaSuccess) {
+    cudaGetLastError();
+    return HEXLIB_B200_ERR_CUDA;
+  }
+  return HEXLIB_B200_OK;
+}
+
+bool aligned16(const void* p) {
+  return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+}  // namespace
+
+int gemm_kernels_init() {
+  cudaError_t e1 = cudaFuncSetAttribute(
+      gemm_f16_tc<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      GemmCfg<64>::SMEM_BYTES);
+  cudaError_t e2 = cudaFuncSetAttribute(
+      gemm_f16_tc<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      GemmCfg<128>::SMEM_BYTES);
+  cudaError_t e3 = cudaFuncSetAttribute(
+      gemm_f16_tc<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      GemmCfg<256>::SMEM_BYTES);
+  sm_count();
+  if (e1 != cudaSuccess || e2 != cudaSuccess || e3 != cudaSuccess) {
+    cudaGetLastError();
+    return HEXLIB_B200_ERR_CUDA;
+  }
+  return HEXLIB_B200_OK;
+}
+
+int launch_gemm(const GemmDesc& g, int* err, cudaStream_t s) {
+  if (g.batch < 0 || g.M < 0 || g.K <= 0 || g.N <= 0 || g.act < 0 ||
+      g.act > 2 || !g.A || !g.B || !g.out)
+    return HEXLIB_B200_ERR_INVAL_PARAMS;
+  if (g.batch == 0 || g.M == 0) return HEXLIB_B200_OK;
+  const bool tma_ok = (g.K % 8) == 0 && (g.N % 8) == 0 && aligned16(g.A) &&
+                      aligned16(g.B) && aligned16(g.out) &&
+                      (!g.bias || aligned16(g.bias)) &&
+                      (!g.resid || aligned16(g.resid)) && tma_available();
+  if (tma_ok) {
+    int rc;
+    if (g.N % 256 == 0)
+      rc = launch_tc<256>(g, err, s);
+    else if (g.N % 128 == 0)
+      rc = launch_tc<128>(g, err, s);
+    else
+      rc = launch_tc<64>(g, err, s);
+    if (rc != -1) return rc;
+    // The tensor map was refused on the host: fall through to CUDA cores.
+  }
+  const int tiles_m = (int)((g.M + 63) / 64), tiles_n = (g.N + 63) / 64;
+  int64_t total = g.batch * tiles_m * (int64_t)tiles_n;
+  int64_t cap = (int64_t)sm_count() * 4;
+  const int grid = (int)(total < cap ? total : cap);
+  gemm_f16_simt<<<grid, 256, 0, s>>>(
+      reinterpret_cast<const __half*>(g.A), reinterpret_cast<const __half*>(g.B),
+      g.bias, reinterpret_cast<const __half*>(g.resid),
+      reinterpret_cast<__half*>(g.out), g.M, g.K, g.N, g.batch,
+      g.b_shared ? 1 : 0, g.act);
+  if (cudaPeekAtLastError() != cudaSuccess) {
+    cudaGetLastError();
+    return HEXLIB_B200_ERR_CUDA;
+  }
+  return HEXLIB_B200_OK;
+}
+
+}  // namespace hb

@@ -1,0 +1,929 @@
+// k_memory.cu -- the memory-bound kernels: elementwise (add, scale, cast),
+// row reductions (layernorm, rmsnorm, softmax), rope_2d, both transposes and
+// patchify.
+//
+// Each one is HBM-bound: it reads every input once and writes every output
+// once, so the target is the copy bandwidth of the part. The common shape is
+// 16-byte vector loads and stores, grid-stride loops over a grid sized in
+// multiples of the SM count, and warp-shuffle reductions with the row held in
+// registers. Arithmetic is fp32 with one rounding to fp16 per output, which
+// is the contract every kernels/<k>/kernel_api.h states.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "hb_kernels.h"
+
+namespace hb {
+namespace {
+
+constexpr int kThreads = 256;
+
+int grid_for(int64_t work_items, int threads) {
+  static int sm_count = 0;
+  if (sm_count == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev);
+    if (sm_count <= 0) sm_count = 148;
+  }
+  int64_t blocks = (work_items + threads - 1) / threads;
+  const int64_t cap = static_cast<int64_t>(sm_count) * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return static_cast<int>(blocks);
+}
+
+bool aligned16(const void* p) {
+  return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+union H8 {
+  uint4 u;
+  __half2 h2[4];
+};
+
+// ---- add -------------------------------------------------------------------
+// y[i] = fp16(float(a[i]) + float(b[i % nb]))   (kernels/add_fp16/kernel_api.h)
+
+__global__ void add_f16_vec(const uint4* __restrict__ a,
+                            const uint4* __restrict__ b, uint4* __restrict__ y,
+                            int64_t nvec, int64_t nbvec) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nvec;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    H8 va, vb, vy;
+    va.u = __ldg(a + i);
+    vb.u = __ldg(b + (nbvec == nvec ? i : i % nbvec));
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 fa = __half22float2(va.h2[j]);
+      float2 fb = __half22float2(vb.h2[j]);
+      vy.h2[j] = __floats2half2_rn(fa.x + fb.x, fa.y + fb.y);
+    }
+    y[i] = vy.u;
+  }
+}
+
+__global__ void add_f16_scalar(const __half* __restrict__ a,
+                               const __half* __restrict__ b,
+                               __half* __restrict__ y, int64_t n, int64_t nb) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    y[i] = __float2half_rn(__half2float(a[i]) + __half2float(b[i % nb]));
+  }
+}
+
+// fp16 + fp32 -> fp16, one rounding.
+__global__ void add_f16_f32_vec(const uint4* __restrict__ a,
+                                const float4* __restrict__ b,
+                                uint4* __restrict__ y, int64_t nvec,
+                                int64_t nbvec) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nvec;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    H8 va, vy;
+    va.u = __ldg(a + i);
+    const int64_t bi = (nbvec == nvec ? i : i % nbvec);
+    float4 b0 = __ldg(b + 2 * bi);
+    float4 b1 = __ldg(b + 2 * bi + 1);
+    float fb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 fa = __half22float2(va.h2[j]);
+      vy.h2[j] = __floats2half2_rn(fa.x + fb[2 * j], fa.y + fb[2 * j + 1]);
+    }
+    y[i] = vy.u;
+  }
+}
+
+__global__ void add_f16_f32_scalar(const __half* __restrict__ a,
+                                   const float* __restrict__ b,
+                                   __half* __restrict__ y, int64_t n,
+                                   int64_t nb) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    y[i] = __float2half_rn(__half2float(a[i]) + b[i % nb]);
+  }
+}
+
+// ---- scale -----------------------------------------------------------------
+// y[i] = fp16(float(x[i]) * factor)   (kernels/scale_fp16/kernel_api.h)
+
+__global__ void scale_f16_vec(const uint4* __restrict__ x,
+                              uint4* __restrict__ y, int64_t nvec,
+                              float factor) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nvec;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    H8 v, o;
+    v.u = __ldg(x + i);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 f = __half22float2(v.h2[j]);
+      o.h2[j] = __floats2half2_rn(__fmul_rn(f.x, factor),
+                                  __fmul_rn(f.y, factor));
+    }
+    y[i] = o.u;
+  }
+}
+
+__global__ void scale_f16_scalar(const __half* __restrict__ x,
+                                 __half* __restrict__ y, int64_t n,
+                                 float factor) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    y[i] = __float2half_rn(__fmul_rn(__half2float(x[i]), factor));
+  }
+}
+
+// ---- cast ------------------------------------------------------------------
+// y[i] = fp16(x[i]), round to nearest even (kernels/cast_f32_f16/kernel_api.h)
+
+__global__ void cast_f32_f16_vec(const float4* __restrict__ x,
+                                 uint4* __restrict__ y, int64_t nvec) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nvec;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float4 a = __ldg(x + 2 * i);
+    float4 b = __ldg(x + 2 * i + 1);
+    H8 o;
+    o.h2[0] = __floats2half2_rn(a.x, a.y);
+    o.h2[1] = __floats2half2_rn(a.z, a.w);
+    o.h2[2] = __floats2half2_rn(b.x, b.y);
+    o.h2[3] = __floats2half2_rn(b.z, b.w);
+    y[i] = o.u;
+  }
+}
+
+__global__ void cast_f32_f16_scalar(const float* __restrict__ x,
+                                    __half* __restrict__ y, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    y[i] = __float2half_rn(x[i]);
+  }
+}
+
+__global__ void copy_vec(const uint4* __restrict__ x, uint4* __restrict__ y,
+                         int64_t nvec) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nvec;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    y[i] = __ldg(x + i);
+  }
+}
+
+__global__ void copy_bytes(const uint8_t* __restrict__ x,
+                           uint8_t* __restrict__ y, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    y[i] = x[i];
+  }
+}
+
+// ---- warp reductions ---------------------------------------------------------
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// ---- layernorm ----------------------------------------------------------------
+// One warp per row, the row held in registers as VPL 16-byte vectors per lane
+// (C = 256 * VPL). Two passes over the registers: the mean, then the biased
+// variance of the centred values (kernels/layernorm_fp16/kernel_api.h:7-29).
+
+template <int VPL>
+__global__ void layernorm_f16_reg(const uint4* __restrict__ x,
+                                  const float* __restrict__ w,
+                                  const float* __restrict__ b,
+                                  uint4* __restrict__ y, int64_t R, float eps) {
+  constexpr int C = VPL * 256;
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t r = warp0; r < R; r += nwarps) {
+    const uint4* xr = x + r * (C / 8);
+    float v[VPL][8];
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      H8 h;
+      h.u = __ldg(xr + j * 32 + lane);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float2 f = __half22float2(h.h2[q]);
+        v[j][2 * q] = f.x;
+        v[j][2 * q + 1] = f.y;
+      }
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j)
+#pragma unroll
+      for (int q = 0; q < 8; ++q) s += v[j][q];
+    const float mean = warp_sum(s) * (1.0f / C);
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j)
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float d = v[j][q] - mean;
+        ss += d * d;
+      }
+    const float var = warp_sum(ss) * (1.0f / C);
+    const float inv = 1.0f / sqrtf(var + eps);
+    uint4* yr = y + r * (C / 8);
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int c0 = (j * 32 + lane) * 8;
+      const float4 w0 = __ldg(reinterpret_cast<const float4*>(w + c0));
+      const float4 w1 = __ldg(reinterpret_cast<const float4*>(w + c0 + 4));
+      const float4 b0 = __ldg(reinterpret_cast<const float4*>(b + c0));
+      const float4 b1 = __ldg(reinterpret_cast<const float4*>(b + c0 + 4));
+      const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+      H8 o;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float o0 = (v[j][2 * q] - mean) * inv * ww[2 * q] + bb[2 * q];
+        const float o1 =
+            (v[j][2 * q + 1] - mean) * inv * ww[2 * q + 1] + bb[2 * q + 1];
+        o.h2[q] = __floats2half2_rn(o0, o1);
+      }
+      yr[j * 32 + lane] = o.u;
+    }
+  }
+}
+
+// Any C: one warp per row, three passes over global memory.
+__global__ void layernorm_f16_generic(const __half* __restrict__ x,
+                                      const float* __restrict__ w,
+                                      const float* __restrict__ b,
+                                      __half* __restrict__ y, int64_t R, int C,
+                                      float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t r = warp0; r < R; r += nwarps) {
+    const __half* xr = x + r * C;
+    float s = 0.f;
+    for (int c = lane; c < C; c += 32) s += __half2float(xr[c]);
+    const float mean = warp_sum(s) / (float)C;
+    float ss = 0.f;
+    for (int c = lane; c < C; c += 32) {
+      const float d = __half2float(xr[c]) - mean;
+      ss += d * d;
+    }
+    const float var = warp_sum(ss) / (float)C;
+    const float inv = 1.0f / sqrtf(var + eps);
+    for (int c = lane; c < C; c += 32)
+      y[r * C + c] =
+          __float2half_rn((__half2float(xr[c]) - mean) * inv * w[c] + b[c]);
+  }
+}
+
+// ---- rmsnorm -------------------------------------------------------------------
+// y = fp16(x * (1/sqrt(mean(x^2) + eps)) * w), w fp16
+// (kernels/rmsnorm_fp16/kernel_api.h:8-14).
+
+template <int VPL>
+__global__ void rmsnorm_f16_reg(const uint4* __restrict__ x,
+                                const uint4* __restrict__ w,
+                                uint4* __restrict__ y, int64_t R, float eps) {
+  constexpr int C = VPL * 256;
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t r = warp0; r < R; r += nwarps) {
+    const uint4* xr = x + r * (C / 8);
+    float v[VPL][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      H8 h;
+      h.u = __ldg(xr + j * 32 + lane);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float2 f = __half22float2(h.h2[q]);
+        v[j][2 * q] = f.x;
+        v[j][2 * q + 1] = f.y;
+        ss += f.x * f.x + f.y * f.y;
+      }
+    }
+    const float inv = 1.0f / sqrtf(warp_sum(ss) * (1.0f / C) + eps);
+    uint4* yr = y + r * (C / 8);
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      H8 hw, o;
+      hw.u = __ldg(w + j * 32 + lane);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 fw = __half22float2(hw.h2[q]);
+        o.h2[q] = __floats2half2_rn(v[j][2 * q] * inv * fw.x,
+                                    v[j][2 * q + 1] * inv * fw.y);
+      }
+      yr[j * 32 + lane] = o.u;
+    }
+  }
+}
+
+__global__ void rmsnorm_f16_generic(const __half* __restrict__ x,
+                                    const __half* __restrict__ w,
+                                    __half* __restrict__ y, int64_t R, int C,
+                                    float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t r = warp0; r < R; r += nwarps) {
+    const __half* xr = x + r * C;
+    float ss = 0.f;
+    for (int c = lane; c < C; c += 32) {
+      const float f = __half2float(xr[c]);
+      ss += f * f;
+    }
+    const float inv = 1.0f / sqrtf(warp_sum(ss) / (float)C + eps);
+    for (int c = lane; c < C; c += 32)
+      y[r * C + c] =
+          __float2half_rn(__half2float(xr[c]) * inv * __half2float(w[c]));
+  }
+}
+
+// ---- softmax --------------------------------------------------------------------
+// Row softmax: max, exp of the shifted values, sum, divide; fp32 throughout
+// and one rounding (kernels/softmax_fp16/kernel_api.h:9-16). One warp per
+// row with the row in registers for C = 256 * VPL.
+
+template <int VPL>
+__global__ void softmax_f16_reg(const uint4* __restrict__ x,
+                                uint4* __restrict__ y, int64_t R) {
+  constexpr int C = VPL * 256;
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t r = warp0; r < R; r += nwarps) {
+    const uint4* xr = x + r * (C / 8);
+    float v[VPL][8];
+    float m = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      H8 h;
+      h.u = __ldg(xr + j * 32 + lane);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float2 f = __half22float2(h.h2[q]);
+        v[j][2 * q] = f.x;
+        v[j][2 * q + 1] = f.y;
+        m = fmaxf(m, fmaxf(f.x, f.y));
+      }
+    }
+    m = warp_max(m);
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j)
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        v[j][q] = expf(v[j][q] - m);
+        s += v[j][q];
+      }
+    const float sum = warp_sum(s);
+    uint4* yr = y + r * (C / 8);
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      H8 o;
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        o.h2[q] = __floats2half2_rn(v[j][2 * q] / sum, v[j][2 * q + 1] / sum);
+      yr[j * 32 + lane] = o.u;
+    }
+  }
+}
+
+__global__ void softmax_f16_generic(const __half* __restrict__ x,
+                                    __half* __restrict__ y, int64_t R, int C) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t r = warp0; r < R; r += nwarps) {
+    const __half* xr = x + r * C;
+    float m = -INFINITY;
+    for (int c = lane; c < C; c += 32) m = fmaxf(m, __half2float(xr[c]));
+    m = warp_max(m);
+    float s = 0.f;
+    for (int c = lane; c < C; c += 32) s += expf(__half2float(xr[c]) - m);
+    const float sum = warp_sum(s);
+    for (int c = lane; c < C; c += 32)
+      y[r * C + c] = __float2half_rn(expf(__half2float(xr[c]) - m) / sum);
+  }
+}
+
+// ---- rope_2d ---------------------------------------------------------------------
+// Split-half rotation (kernels/rope_2d_fp16/kernel_api.h:17-26):
+//   y[i]      = x[i]      * cos[i]      - x[i+h] * sin[i]
+//   y[i + h]  = x[i + h]  * cos[i + h]  + x[i]   * sin[i + h]
+// evaluated as the op registry does (structural.py:249-254): the two products
+// rounded to fp32 separately, then added, so no fused multiply-add changes a
+// rounding. One thread per 8 columns of the first half of one (token, head).
+
+__global__ void rope_f16_vec(const uint4* __restrict__ x,
+                             const float* __restrict__ cos_t,
+                             const float* __restrict__ sin_t,
+                             uint4* __restrict__ y, int64_t rows, int H, int D,
+                             int64_t table_rows) {
+  const int half = D >> 1;
+  const int cpr = half >> 3;  // 8-wide chunks per half
+  const int64_t total = rows * H * cpr;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int c = (int)(i % cpr);
+    const int64_t th = i / cpr;  // token * H + head
+    const int64_t t = th / H;
+    const int64_t tt = t % table_rows;
+    const int64_t base = th * D;  // element offset of this (token, head)
+    const int i0 = c * 8;
+    H8 lo, hi, olo, ohi;
+    lo.u = __ldg(x + (base + i0) / 8);
+    hi.u = __ldg(x + (base + half + i0) / 8);
+    const float* ct = cos_t + tt * D;
+    const float* st = sin_t + tt * D;
+    const float4 c0 = __ldg(reinterpret_cast<const float4*>(ct + i0));
+    const float4 c1 = __ldg(reinterpret_cast<const float4*>(ct + i0 + 4));
+    const float4 c2 = __ldg(reinterpret_cast<const float4*>(ct + half + i0));
+    const float4 c3 =
+        __ldg(reinterpret_cast<const float4*>(ct + half + i0 + 4));
+    const float4 s0 = __ldg(reinterpret_cast<const float4*>(st + i0));
+    const float4 s1 = __ldg(reinterpret_cast<const float4*>(st + i0 + 4));
+    const float4 s2 = __ldg(reinterpret_cast<const float4*>(st + half + i0));
+    const float4 s3 =
+        __ldg(reinterpret_cast<const float4*>(st + half + i0 + 4));
+    const float cl[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    const float ch[8] = {c2.x, c2.y, c2.z, c2.w, c3.x, c3.y, c3.z, c3.w};
+    const float sl[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    const float sh[8] = {s2.x, s2.y, s2.z, s2.w, s3.x, s3.y, s3.z, s3.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 a = __half22float2(lo.h2[q]);
+      const float2 b = __half22float2(hi.h2[q]);
+      const float ylo0 = __fadd_rn(__fmul_rn(a.x, cl[2 * q]),
+                                   __fmul_rn(-b.x, sl[2 * q]));
+      const float ylo1 = __fadd_rn(__fmul_rn(a.y, cl[2 * q + 1]),
+                                   __fmul_rn(-b.y, sl[2 * q + 1]));
+      const float yhi0 = __fadd_rn(__fmul_rn(b.x, ch[2 * q]),
+                                   __fmul_rn(a.x, sh[2 * q]));
+      const float yhi1 = __fadd_rn(__fmul_rn(b.y, ch[2 * q + 1]),
+                                   __fmul_rn(a.y, sh[2 * q + 1]));
+      olo.h2[q] = __floats2half2_rn(ylo0, ylo1);
+      ohi.h2[q] = __floats2half2_rn(yhi0, yhi1);
+    }
+    y[(base + i0) / 8] = olo.u;
+    y[(base + half + i0) / 8] = ohi.u;
+  }
+}
+
+__global__ void rope_f16_scalar(const __half* __restrict__ x,
+                                const float* __restrict__ cos_t,
+                                const float* __restrict__ sin_t,
+                                __half* __restrict__ y, int64_t rows, int H,
+                                int D, int64_t table_rows) {
+  const int half = D >> 1;
+  const int64_t total = rows * H * half;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int j = (int)(i % half);
+    const int64_t th = i / half;
+    const int64_t tt = (th / H) % table_rows;
+    const int64_t base = th * D;
+    const float a = __half2float(x[base + j]);
+    const float b = __half2float(x[base + half + j]);
+    const float* ct = cos_t + tt * D;
+    const float* st = sin_t + tt * D;
+    y[base + j] = __float2half_rn(
+        __fadd_rn(__fmul_rn(a, ct[j]), __fmul_rn(-b, st[j])));
+    y[base + half + j] = __float2half_rn(
+        __fadd_rn(__fmul_rn(b, ct[half + j]), __fmul_rn(a, st[half + j])));
+  }
+}
+
+// ---- transpose_th: [T,H,D] -> [H,T,D] per image ----------------------------------
+// D is innermost on both sides, so the op moves whole D-runs: one thread per
+// 16-byte vector, coalesced on both sides.
+
+__global__ void transpose_th_vec(const uint4* __restrict__ x,
+                                 uint4* __restrict__ y, int64_t nimg, int T,
+                                 int H, int DV) {
+  const int64_t per = (int64_t)T * H * DV;
+  const int64_t total = nimg * per;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t img = i / per;
+    int64_t r = i - img * per;  // index in the OUTPUT [H,T,DV]
+    const int dv = (int)(r % DV);
+    r /= DV;
+    const int t = (int)(r % T);
+    const int h = (int)(r / T);
+    y[i] = __ldg(x + img * per + ((int64_t)t * H + h) * DV + dv);
+  }
+}
+
+__global__ void transpose_th_scalar(const __half* __restrict__ x,
+                                    __half* __restrict__ y, int64_t nimg,
+                                    int T, int H, int D) {
+  const int64_t per = (int64_t)T * H * D;
+  const int64_t total = nimg * per;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t img = i / per;
+    int64_t r = i - img * per;
+    const int d = (int)(r % D);
+    r /= D;
+    const int t = (int)(r % T);
+    const int h = (int)(r / T);
+    y[i] = x[img * per + ((int64_t)t * H + h) * D + d];
+  }
+}
+
+// ---- transpose_hd: [B,T,D] -> [B,D,T] ---------------------------------------------
+// 64x64 tiles through shared memory (padded against bank conflicts): both
+// the read of T x D rows and the write of D x T rows are coalesced.
+
+constexpr int kTile = 64;
+
+__global__ void transpose_hd_tiled(const __half* __restrict__ x,
+                                   __half* __restrict__ y, int64_t B, int T,
+                                   int D) {
+  __shared__ __half tile[kTile][kTile + 2];
+  const int tiles_t = (T + kTile - 1) / kTile;
+  const int tiles_d = (D + kTile - 1) / kTile;
+  const int64_t ntiles = B * tiles_t * tiles_d;
+  for (int64_t tid = blockIdx.x; tid < ntiles; tid += gridDim.x) {
+    const int64_t b = tid / ((int64_t)tiles_t * tiles_d);
+    const int rem = (int)(tid - b * tiles_t * tiles_d);
+    const int t0 = (rem / tiles_d) * kTile;
+    const int d0 = (rem % tiles_d) * kTile;
+    const __half* xb = x + b * (int64_t)T * D;
+    __half* yb = y + b * (int64_t)T * D;
+    // load: rows t, columns d (d fastest across threads)
+    for (int e = threadIdx.x; e < kTile * kTile; e += blockDim.x) {
+      const int tr = e / kTile, dc = e % kTile;
+      const int t = t0 + tr, d = d0 + dc;
+      if (t < T && d < D) tile[tr][dc] = xb[(int64_t)t * D + d];
+    }
+    __syncthreads();
+    // store: rows d, columns t (t fastest across threads)
+    for (int e = threadIdx.x; e < kTile * kTile; e += blockDim.x) {
+      const int dr = e / kTile, tc = e % kTile;
+      const int t = t0 + tc, d = d0 + dr;
+      if (t < T && d < D) yb[(int64_t)d * T + t] = tile[tc][dr];
+    }
+    __syncthreads();
+  }
+}
+
+// ---- patchify ---------------------------------------------------------------------
+// [C,T,H,W] -> [gh*gw, C*T*p*p] in merge-block token order
+// (kernels/patchify_fp32/kernel_api.h:18-38; structural.py:172-207):
+//   token = ((bh*Bw + bw)*merge + mh)*merge + mw,  gh = bh*merge + mh, ...
+//   feature = ((c*T + t)*p + ph)*p + pw
+// One thread per output float4 (4 consecutive pw): a pure, bit-exact move.
+
+__global__ void patchify_vec(const float4* __restrict__ img,
+                             float4* __restrict__ out, int64_t nimg, int C,
+                             int T, int H, int W, int patch, int merge,
+                             int grid_w) {
+  const int feat = C * T * patch * patch;
+  const int fv = feat / 4;
+  const int ntok = (H / patch) * grid_w;
+  const int64_t per = (int64_t)ntok * fv;
+  const int64_t total = nimg * per;
+  const int bw_n = grid_w / merge;
+  const int pv = patch / 4;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t n = i / per;
+    const int64_t r = i - n * per;
+    const int tok = (int)(r / fv);
+    const int f4 = (int)(r % fv);
+    const int pw4 = f4 % pv;
+    int q = f4 / pv;
+    const int ph = q % patch;
+    q /= patch;
+    const int t = q % T;
+    const int c = q / T;
+    const int mw = tok % merge;
+    int u = tok / merge;
+    const int mh = u % merge;
+    u /= merge;
+    const int bw = u % bw_n;
+    const int bh = u / bw_n;
+    const int gh = bh * merge + mh, gw = bw * merge + mw;
+    const int h = gh * patch + ph;
+    const int64_t src =
+        ((((n * C + c) * T + t) * (int64_t)H + h) * W + gw * patch) / 4 + pw4;
+    out[i] = __ldg(img + src);
+  }
+}
+
+__global__ void patchify_scalar(const float* __restrict__ img,
+                                float* __restrict__ out, int64_t nimg, int C,
+                                int T, int H, int W, int patch, int merge,
+                                int grid_w) {
+  const int feat = C * T * patch * patch;
+  const int ntok = (H / patch) * grid_w;
+  const int64_t per = (int64_t)ntok * feat;
+  const int64_t total = nimg * per;
+  const int bw_n = grid_w / merge;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t n = i / per;
+    const int64_t r = i - n * per;
+    const int tok = (int)(r / feat);
+    const int f = (int)(r % feat);
+    const int pw = f % patch;
+    int q = f / patch;
+    const int ph = q % patch;
+    q /= patch;
+    const int t = q % T;
+    const int c = q / T;
+    const int mw = tok % merge;
+    int u = tok / merge;
+    const int mh = u % merge;
+    u /= merge;
+    const int bw = u % bw_n;
+    const int bh = u / bw_n;
+    const int gh = bh * merge + mh, gw = bw * merge + mw;
+    out[i] = img[(((n * C + c) * T + t) * (int64_t)H + gh * patch + ph) * W +
+                 gw * patch + pw];
+  }
+}
+
+}  // namespace
+
+// ---- launchers ------------------------------------------------------------------
+
+// Load every kernel of this file now, so that no module load happens lazily
+// inside a CUDA-graph capture.
+int memory_kernels_init() {
+  const void* fns[] = {
+      (const void*)add_f16_vec,         (const void*)add_f16_scalar,
+      (const void*)add_f16_f32_vec,     (const void*)add_f16_f32_scalar,
+      (const void*)scale_f16_vec,       (const void*)scale_f16_scalar,
+      (const void*)cast_f32_f16_vec,    (const void*)cast_f32_f16_scalar,
+      (const void*)copy_vec,            (const void*)copy_bytes,
+      (const void*)layernorm_f16_reg<1>, (const void*)layernorm_f16_reg<2>,
+      (const void*)layernorm_f16_reg<3>, (const void*)layernorm_f16_reg<4>,
+      (const void*)layernorm_f16_generic,
+      (const void*)rmsnorm_f16_reg<1>,  (const void*)rmsnorm_f16_reg<2>,
+      (const void*)rmsnorm_f16_reg<3>,  (const void*)rmsnorm_f16_reg<4>,
+      (const void*)rmsnorm_f16_reg<16>, (const void*)rmsnorm_f16_generic,
+      (const void*)softmax_f16_reg<1>,  (const void*)softmax_f16_reg<2>,
+      (const void*)softmax_f16_reg<3>,  (const void*)softmax_f16_reg<4>,
+      (const void*)softmax_f16_reg<8>,  (const void*)softmax_f16_reg<16>,
+      (const void*)softmax_f16_generic, (const void*)rope_f16_vec,
+      (const void*)rope_f16_scalar,     (const void*)transpose_th_vec,
+      (const void*)transpose_th_scalar, (const void*)transpose_hd_tiled,
+      (const void*)patchify_vec,        (const void*)patchify_scalar,
+  };
+  for (const void* f : fns) {
+    cudaFuncAttributes attr;
+    if (cudaFuncGetAttributes(&attr, f) != cudaSuccess) {
+      cudaGetLastError();
+      return HEXLIB_B200_ERR_CUDA;
+    }
+  }
+  grid_for(1, kThreads);
+  return HEXLIB_B200_OK;
+}
+
+#define HB_LAUNCH_CHECK()                                           \
+  do {                                                                \
+    if (cudaPeekAtLastError() != cudaSuccess) {                       \
+      cudaGetLastError();                                             \
+      return HEXLIB_B200_ERR_CUDA;                                    \
+    }                                                                 \
+    return HEXLIB_B200_OK;                                            \
+  } while (0)
+
+int launch_add_f16(const void* a, const void* b, void* y, int64_t n,
+                   int64_t nb, cudaStream_t s) {
+  if (n < 0 || nb <= 0 || (n > 0 && n % nb != 0))
+    return HEXLIB_B200_ERR_INVAL_PARAMS;
+  if (n == 0) return HEXLIB_B200_OK;
+  if (n % 8 == 0 && nb % 8 == 0 && aligned16(a) && aligned16(b) &&
+      aligned16(y)) {
+    const int64_t nv = n / 8;
+    add_f16_vec<<<grid_for(nv, kThreads), kThreads, 0, s>>>(
+        (const uint4*)a, (const uint4*)b, (uint4*)y, nv, nb / 8);
+  } else {
+    add_f16_scalar<<<grid_for(n, kThreads), kThreads, 0, s>>>(
+        (const __half*)a, (const __half*)b, (__half*)y, n, nb);
+  }
+  HB_LAUNCH_CHECK();
+}
+
+int launch_add_f16_f32(const void* a, const float* b, void* y, int64_t n,
+                       int64_t nb, cudaStream_t s) {
+  if (n < 0 || nb <= 0 || (n > 0 && n % nb != 0))
+    return HEXLIB_B200_ERR_INVAL_PARAMS;
+  if (n == 0) return HEXLIB_B200_OK;
+  if (n % 8 == 0 && nb % 8 == 0 && aligned16(a) && aligned16(b) &&
+      aligned16(y)) {
+    const int64_t nv = n / 8;
+    add_f16_f32_vec<<<grid_for(nv, kThreads), kThreads, 0, s>>>(
+        (const uint4*)a, (const float4*)b, (uint4*)y, nv, nb / 8);
+  } else {
+    add_f16_f32_scalar<<<grid_for(n, kThreads), kThreads, 0, s>>>(
+        (const __half*)a, b, (__half*)y, n, nb);
+  }
+  HB_LAUNCH_CHECK();
+}
+
+int launch_cast_f32_f16(const float* x, void* y, int64_t n, cudaStream_t s) {
+  if (n < 0) return HEXLIB_B200_ERR_INVAL_PARAMS;
+  if (n == 0) return HEXLIB_B200_OK;
+  if (n % 8 == 0 && aligned16(x) && aligned16(y)) {
+    const int64_t nv = n / 8;
+    cast_f32_f16_vec<<<grid_for(nv, kThreads), kThreads, 0, s>>>(
+        (const float4*)x, (uint4*)y, nv);
+  } else {
+    cast_f32_f16_scalar<<<grid_for(n, kThreads), kThreads, 0, s>>>(
+        x, (__half*)y, n);
+  }
+  HB_LAUNCH_CHECK();
+}
+
+int launch_scale_f16(const void* x, void* y, int64_t n, float factor,
+                     cudaStream_t s) {
+  if (n < 0) return HEXLIB_B200_ERR_INVAL_PARAMS;
+  if (n == 0) return HEXLIB_B200_OK;
+  if (n % 8 == 0 && aligned16(x) && aligned16(y)) {
+    const int64_t nv = n / 8;
+    scale_f16_vec<<<grid_for(nv, kThreads), kThreads, 0, s>>>(
+        (const uint4*)x, (uint4*)y, nv, factor);
+  } else {
+    scale_f16_scalar<<<grid_for(n, kThreads), kThreads, 0, s>>>(
+        (const __half*)x, (__half*)y, n, factor);
+  }
+  HB_LAUNCH_CHECK();
+}
+
+int launch_copy(const void* x, void* y, int64_t nbytes, cudaStream_t s) {
+  if (nbytes < 0) return HEXLIB_B200_ERR_INVAL_PARAMS;
+  if (nbytes == 0 || x == y) return HEXLIB_B200_OK;
+  if (nbytes % 16 == 0 && aligned16(x) && aligned16(y)) {
+    const int64_t nv = nbytes / 16;
+    copy_vec<<<grid_for(nv, kThreads), kThreads, 0, s>>>((const uint4*)x,
+                                                         (uint4*)y, nv);
+  } else {
+    copy_bytes<<<grid_for(nbytes, kThreads), kThreads, 0, s>>>(
+        (const uint8_t*)x, (uint8_t*)y, nbytes);
+  }
+  HB_LAUNCH_CHECK();
+}
+
+int launch_layernorm_f16(const void* x, const float* w, const float* b,
+                         void* y, int64_t R, int C, float eps, cudaStream_t s) {
+  if (R < 0 || C <= 0) return HEXLIB_B200_ERR_INVAL_PARAMS;
+  if (R == 0) return HEXLIB_B200_OK;
+  const bool al = aligned16(x) && aligned16(y) && aligned16(w) && aligned16(b);
+  const int grid = grid_for(R * 32, kThreads);
+  if (al && C == 256)
+    layernorm_f16_reg<1><<<grid, kThreads, 0, s>>>(
+        (const uint4*)x, w, b, (uint4*)y, R, eps);
+  else if (al && C == 512)
+    layernorm_f16_reg<2><<<grid, kThreads, 0, s>>>(
+        (const uint4*)x, w, b, (uint4*)y, R, eps);
+  else if (al && C == 768)
+    layernorm_f16_reg<3><<<grid, kThreads, 0, s>>>(
+        (const uint4*)x, w, b, (uint4*)y, R, eps);
+  else if (al && C == 1024)
+    layernorm_f16_reg<4><<<grid, kThreads, 0, s>>>(
+        (const uint4*)x, w, b, (uint4*)y, R, eps);
+  else
+    layernorm_f16_generic<<<grid, kThreads, 0, s>>>(
+        (const __half*)x, w, b, (__half*)y, R, C, eps);
+  HB_LAUNCH_CHECK();
+}
+
+int launch_rmsnorm_f16(const void* x, const void* w, void* y, int64_t R, int C,
+                       float eps, cudaStream_t s) {
+  if (R < 0 || C <= 0) return HEXLIB_B200_ERR_INVAL_PARAMS;
+  if (R == 0) return HEXLIB_B200_OK;
+  const bool al = aligned16(x) && aligned16(y) && aligned16(w);
+  const int grid = grid_for(R * 32, kThreads);
+  if (al && C == 256)
+    rmsnorm_f16_reg<1><<<grid, kThreads, 0, s>>>(
+        (const uint4*)x, (const uint4*)w, (uint4*)y, R, eps);
+  else if (al && C == 512)
+    rmsnorm_f16_reg<2><<<grid, kThreads, 0, s>>>(
+        (const uint4*)x, (const uint4*)w, (uint4*)y, R, eps);
+  else if (al && C == 768)
+    rmsnorm_f16_reg<3><<<grid, kThreads, 0, s>>>(
+        (const uint4*)x, (const uint4*)w, (uint4*)y, R, eps);
+  else if (al && C == 1024)
+    rmsnorm_f16_reg<4><<<grid, kThreads, 0, s>>>(
+        (const uint4*)x, (const uint4*)w, (uint4*)y, R, eps);
+  else if (al && C == 4096)
+    rmsnorm_f16_reg<16><<<grid, kThreads, 0, s>>>(
+        (const uint4*)x, (const uint4*)w, (uint4*)y, R, eps);
+  else
+    rmsnorm_f16_generic<<<grid, kThreads, 0, s>>>(
+        (const __half*)x, (const __half*)w, (__half*)y, R, C, eps);
+  HB_LAUNCH_CHECK();
+}
+
+int launch_softmax_f16(const void* x, void* y, int64_t R, int C,
+                       cudaStream_t s) {
+  if (R < 0 || C <= 0) return HEXLIB_B200_ERR_INVAL_PARAMS;
+  if (R == 0) return HEXLIB_B200_OK;
+  const bool al = aligned16(x) && aligned16(y);
+  const int grid = grid_for(R * 32, kThreads);
+  if (al && C == 256)
+    softmax_f16_reg<1><<<grid, kThreads, 0, s>>>((const uint4*)x, (uint4*)y, R);
+  else if (al && C == 512)
+    softmax_f16_reg<2><<<grid, kThreads, 0, s>>>((const uint4*)x, (uint4*)y, R);
+  else if (al && C == 768)
+    softmax_f16_reg<3><<<grid, kThreads, 0, s>>>((const uint4*)x, (uint4*)y, R);
+  else if (al && C == 1024)
+    softmax_f16_reg<4><<<grid, kThreads, 0, s>>>((const uint4*)x, (uint4*)y, R);
+  else if (al && C == 2048)
+    softmax_f16_reg<8><<<grid, kThreads, 0, s>>>((const uint4*)x, (uint4*)y, R);
+  else if (al && C == 4096)
+    softmax_f16_reg<16><<<grid, kThreads, 0, s>>>((const uint4*)x, (uint4*)y,
+                                                   R);
+  else
+    softmax_f16_generic<<<grid, kThreads, 0, s>>>((const __half*)x, (__half*)y,
+                                                  R, C);
+  HB_LAUNCH_CHECK();
+}
+
+int launch_rope_f16(const void* x, const float* cos_t, const float* sin_t,
+                    void* y, int64_t rows, int H, int D, int64_t table_rows,
+                    cudaStream_t s) {
+  if (rows < 0 || H <= 0 || D <= 0 || (D & 1) || table_rows <= 0)
+    return HEXLIB_B200_ERR_INVAL_PARAMS;
+  if (rows == 0) return HEXLIB_B200_OK;
+  const bool al = aligned16(x) && aligned16(y) && aligned16(cos_t) &&
+                  aligned16(sin_t);
+  if (al && (D % 16) == 0) {
+    const int64_t total = rows * H * (D / 16);
+    rope_f16_vec<<<grid_for(total, kThreads), kThreads, 0, s>>>(
+        (const uint4*)x, cos_t, sin_t, (uint4*)y, rows, H, D, table_rows);
+  } else {
+    const int64_t total = rows * H * (D / 2);
+    rope_f16_scalar<<<grid_for(total, kThreads), kThreads, 0, s>>>(
+        (const __half*)x, cos_t, sin_t, (__half*)y, rows, H, D, table_rows);
+  }
+  HB_LAUNCH_CHECK();
+}
+
+int launch_transpose_th_f16(const void* x, void* y, int64_t nimg, int T, int H,
+                            int D, cudaStream_t s) {
+  if (nimg < 0 || T <= 0 || H <= 0 || D <= 0)
+    return HEXLIB_B200_ERR_INVAL_PARAMS;
+  if (nimg == 0) return HEXLIB_B200_OK;
+  const int64_t total = nimg * T * H * (int64_t)D;
+  if ((D % 8) == 0 && aligned16(x) && aligned16(y)) {
+    transpose_th_vec<<<grid_for(total / 8, kThreads), kThreads, 0, s>>>(
+        (const uint4*)x, (uint4*)y, nimg, T, H, D / 8);
+  } else {
+    transpose_th_scalar<<<grid_for(total, kThreads), kThreads, 0, s>>>(
+        (const __half*)x, (__half*)y, nimg, T, H, D);
+  }
+  HB_LAUNCH_CHECK();
+}
+
+int launch_transpose_hd_f16(const void* x, void* y, int64_t B, int T, int D,
+                            cudaStream_t s) {
+  if (B < 0 || T <= 0 || D <= 0) return HEXLIB_B200_ERR_INVAL_PARAMS;
+  if (B == 0) return HEXLIB_B200_OK;
+  const int64_t ntiles =
+      B * ((T + kTile - 1) / kTile) * (int64_t)((D + kTile - 1) / kTile);
+  int grid = grid_for(ntiles * kThreads, kThreads);
+  transpose_hd_tiled<<<grid, kThreads, 0, s>>>((const __half*)x, (__half*)y, B,
+                                               T, D);
+  HB_LAUNCH_CHECK();
+}
+
+int launch_patchify_f32(const float* img, float* out, int64_t nimg, int C,
+                        int T, int H, int W, int patch, int merge, int grid_h,
+                        int grid_w, cudaStream_t s) {
+  if (nimg < 0 || C <= 0 || T <= 0 || patch <= 0 || merge <= 0 ||
+      grid_h <= 0 || grid_w <= 0 || grid_h * patch != H ||
+      grid_w * patch != W || grid_h % merge || grid_w % merge)
+    return HEXLIB_B200_ERR_INVAL_PARAMS;
+  if (nimg == 0) return HEXLIB_B200_OK;
+  const int64_t total =
+      nimg * (int64_t)grid_h * grid_w * C * T * patch * patch;
+  if ((patch % 4) == 0 && aligned16(img) && aligned16(out)) {
+    patchify_vec<<<grid_for(total / 4, kThreads), kThreads, 0, s>>>(
+        (const float4*)img, (float4*)out, nimg, C, T, H, W, patch, merge,
+        grid_w);
+  } else {
+    patchify_scalar<<<grid_for(total, kThreads), kThreads, 0, s>>>(
+        img, out, nimg, C, T, H, W, patch, merge, grid_w);
+  }
+  HB_LAUNCH_CHECK();
+}
+
+}  // namespace hb

@@ -1,0 +1,271 @@
+"""A whole compiled plan -> ONE batch blob for the CUDA dispatcher, over two
+device buffers: the shared consts and a per-image region.
+
+The CUDA analogue of hexlib/exec/wholeplan.py:92-357 (`build_whole_plan_batch`):
+the same walk over the plan's steps, the same variant selection per op
+(`runner.select`), reshapes emitted as no op but as a second tensor descriptor
+on the same bytes, and the same blob format (`wire.pack_batch`). What differs
+is the arena, because the GPU runs B images per launch:
+
+  buffer 0 (fd CONST_FD)   every const, each at its own 256-byte-aligned
+                           offset, staged once per session in the dtype its
+                           consuming kernel takes.
+  buffer 1 (fd IMAGE_FD)   every activation and every graph input/output, at
+                           PER-IMAGE offsets, flagged BUF_PER_IMAGE: with B
+                           images the dispatcher gives each tensor B
+                           contiguous copies, so each kernel sees [B, ...].
+
+`alias=True` lets activations whose lifetimes do not overlap share bytes, with
+liveness computed on the plan's own op order and every reshape chain unified
+into its storage owner first -- the "reshape unification" that the reference's
+builder refuses without (wholeplan.py:235-258, 360-409). Graph inputs and
+outputs are never aliased.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Any, Mapping
+
+import numpy as np
+
+from hexlib_b200 import runner, wire
+from hexlib_b200.graph import as_graph, nbytes as ir_nbytes
+
+CONST_FD = 0
+IMAGE_FD = 1
+ALIGN = 256
+
+_NP = {"fp32": np.float32, "fp16": np.float16, "int32": np.int32}
+
+
+class WholePlanError(Exception):
+    pass
+
+
+def _align(n: int, a: int = ALIGN) -> int:
+    return (n + a - 1) // a * a
+
+
+def _ne(shape) -> tuple[int, int, int, int]:
+    if len(shape) > 4:
+        raise WholePlanError(f"shape {tuple(shape)} has more than 4 dims; ne is fixed at 4")
+    return tuple(int(s) for s in shape) + (1,) * (4 - len(shape))
+
+
+@dataclass(frozen=True)
+class Placement:
+    name: str
+    buffer: int          # CONST_FD or IMAGE_FD
+    offset: int          # per-image offset for IMAGE_FD tensors
+    nbytes: int          # per image
+    dtype: str
+    shape: tuple[int, ...]
+    region: str          # "const" | "act" | "io" | "reshape-alias"
+
+
+@dataclass
+class CudaPlan:
+    blob: bytes
+    const_payload: bytearray | None
+    const_bytes: int
+    image_bytes: int                     # per-image region size
+    placements: dict[str, Placement]
+    index: dict[str, int]                # tensor name -> wire tensor index
+    n_ops: int
+    op_names: tuple[str, ...]
+    inputs: tuple[str, ...]
+    outputs: tuple[str, ...]
+    skipped_reshapes: int
+    kinds: tuple[str, ...] = field(default=())
+
+    def response_capacity(self) -> int:
+        return wire.response_capacity(self.n_ops)
+
+
+def _steps(compiled):
+    for s in compiled.plan.steps:
+        op = getattr(s, "op", None)
+        if op is not None:
+            yield op
+
+
+def _allocate_aliased(names, first, last, size) -> tuple[dict[str, int], int]:
+    """First-fit by decreasing size over [first, last] op-index lifetimes."""
+    placed: list[tuple[int, int, int, int]] = []  # (offset, end, first, last)
+    offs: dict[str, int] = {}
+    for n in sorted(names, key=lambda k: (-size[k], k)):
+        lo, hi, sz = first[n], last[n], size[n]
+        clashes = sorted((o, e) for (o, e, f, l) in placed if f <= hi and lo <= l)
+        cand = 0
+        for o, e in clashes:
+            if cand + sz <= o:
+                break
+            cand = max(cand, _align(e))
+        offs[n] = cand
+        placed.append((cand, cand + sz, lo, hi))
+    end = max((o + size[n] for n, o in offs.items()), default=0)
+    return offs, _align(end)
+
+
+def build_cuda_plan(compiled, feeds: Mapping[str, Any] | None = None,
+                    alias: bool = False) -> CudaPlan:
+    """Pack `compiled`'s whole plan into one blob; stage `feeds`' consts if
+    given. `compiled` is anything with `.graph` and `.plan.steps[i].op`: the
+    reference's `Compiled` or this package's `ExecPlan`."""
+    graph = as_graph(compiled.graph)
+    tensors = graph.tensors
+    order = list(_steps(compiled))
+    if not order:
+        raise WholePlanError("the plan has no ops")
+    io_names = set(graph.inputs) | set(graph.outputs)
+    const_names = {n for n, t in tensors.items() if t.const}
+
+    reshape_src: dict[str, str] = {}
+    for op in order:
+        if op.kind == "reshape":
+            reshape_src[op.outputs[0]] = op.inputs[0]
+
+    def owner(name: str) -> str:
+        seen = {name}
+        while name in reshape_src:
+            name = reshape_src[name]
+            if name in seen:
+                raise WholePlanError(f"reshape chain cycles at {name!r}")
+            seen.add(name)
+        return name
+
+    aliased_io = sorted(n for n in reshape_src if n in io_names)
+    if aliased_io:
+        raise WholePlanError(f"graph inputs/outputs {aliased_io} are reshape outputs; "
+                             "give them their own storage first")
+
+    # ---- select every op's variant and claim dtypes -------------------------
+    specs: dict[int, tuple[str, runner.CudaSpec]] = {}
+    for op in order:
+        if op.kind == "reshape":
+            continue
+        dts = tuple(tensors[n].dtype for n in op.inputs)
+        try:
+            name, spec = runner.select(op.kind, dict(op.attrs), dts)
+            spec.check_requires(dict(op.attrs))
+        except (KeyError, ValueError) as e:
+            raise WholePlanError(f"op {op.id} ({op.kind}): {e}") from e
+        for n in op.outputs:
+            if spec.out_dtype != "any" and tensors[n].dtype != spec.out_dtype:
+                raise WholePlanError(
+                    f"op {op.id} ({op.kind}) writes {n!r} as {tensors[n].dtype}; "
+                    f"the kernel writes {spec.out_dtype}")
+        specs[op.id] = (name, spec)
+
+    def tbytes(n: str) -> int:
+        return ir_nbytes(tensors[n].shape, tensors[n].dtype)
+
+    placements: dict[str, Placement] = {}
+
+    # ---- consts --------------------------------------------------------------
+    cursor = 0
+    used = {n for op in order for n in op.inputs}
+    for n in sorted(const_names):
+        if n not in used:
+            continue
+        t = tensors[n]
+        placements[n] = Placement(n, CONST_FD, cursor, tbytes(n), t.dtype, t.shape, "const")
+        cursor = _align(cursor + tbytes(n))
+    const_bytes = max(cursor, ALIGN)
+
+    # ---- per-image region ------------------------------------------------------
+    act_names = sorted({n for op in order for n in tuple(op.inputs) + tuple(op.outputs)
+                        if n not in const_names and n not in io_names
+                        and n not in reshape_src})
+    cursor = 0
+    io_sorted = sorted(io_names)
+    for n in io_sorted:
+        t = tensors[n]
+        placements[n] = Placement(n, IMAGE_FD, cursor, tbytes(n), t.dtype, t.shape, "io")
+        cursor = _align(cursor + tbytes(n))
+    io_end = cursor
+    if alias:
+        first: dict[str, int] = {}
+        last: dict[str, int] = {}
+        for i, op in enumerate(order):
+            for n in op.outputs:
+                o = owner(n)
+                first.setdefault(o, i)
+                last[o] = max(last.get(o, i), i)
+            for n in op.inputs:
+                o = owner(n)
+                if o in first:
+                    last[o] = max(last[o], i)
+        missing = [n for n in act_names if n not in first]
+        if missing:
+            raise WholePlanError(f"activations read but never written: {missing[:5]}")
+        size = {n: tbytes(n) for n in act_names}
+        offs, span = _allocate_aliased(act_names, first, last, size)
+        for n in act_names:
+            t = tensors[n]
+            placements[n] = Placement(n, IMAGE_FD, io_end + offs[n], size[n], t.dtype,
+                                      t.shape, "act")
+        cursor = io_end + span
+    else:
+        for n in act_names:
+            t = tensors[n]
+            placements[n] = Placement(n, IMAGE_FD, cursor, tbytes(n), t.dtype, t.shape, "act")
+            cursor = _align(cursor + tbytes(n))
+    image_bytes = max(cursor, ALIGN)
+
+    for n in reshape_src:
+        o = owner(n)
+        if o not in placements:
+            raise WholePlanError(f"reshape {n!r} resolves to unplaced {o!r}")
+        base = placements[o]
+        if tbytes(n) != base.nbytes:
+            raise WholePlanError(f"reshape {n!r} changes the byte count")
+        t = tensors[n]
+        placements[n] = Placement(n, base.buffer, base.offset, base.nbytes, t.dtype, t.shape,
+                                  "reshape-alias")
+
+    # ---- stage consts --------------------------------------------------------------
+    payload = None
+    if feeds is not None:
+        payload = bytearray(const_bytes)
+        for n, p in placements.items():
+            if p.region != "const":
+                continue
+            if n not in feeds:
+                raise WholePlanError(f"no feed supplied for const {n!r}")
+            a = np.ascontiguousarray(np.asarray(feeds[n]), dtype=_NP[p.dtype])
+            if tuple(a.shape) != tuple(p.shape):
+                raise WholePlanError(f"feed {n!r} has shape {a.shape}, declared {p.shape}")
+            raw = a.tobytes()
+            payload[p.offset:p.offset + len(raw)] = raw
+
+    # ---- wire descriptors ----------------------------------------------------------
+    names = sorted(placements)
+    index = {n: i for i, n in enumerate(names)}
+    wt = [wire.TensorDesc(bi=0 if placements[n].buffer == CONST_FD else 1,
+                          offset=placements[n].offset, nbytes=placements[n].nbytes,
+                          dtype=placements[n].dtype, layout="row_major",
+                          ne=_ne(placements[n].shape)) for n in names]
+    ops: list[wire.OpDesc] = []
+    op_names: list[str] = []
+    kinds: list[str] = []
+    skipped = 0
+    for op in order:
+        if op.kind == "reshape":
+            skipped += 1
+            continue
+        vname, spec = specs[op.id]
+        ops.append(wire.OpDesc(kind=runner.KIND_ID[vname],
+                               params=runner.encode_params(spec, dict(op.attrs)),
+                               src=tuple(index[n] for n in op.inputs),
+                               dst=tuple(index[n] for n in op.outputs)))
+        op_names.append(f"{op.id}:{vname}")
+        kinds.append(vname)
+    bufs = [wire.BufDesc(fd=CONST_FD, size=const_bytes, flags=0),
+            wire.BufDesc(fd=IMAGE_FD, size=image_bytes, flags=wire.BUF_PER_IMAGE)]
+    blob = wire.pack_batch(bufs, wt, ops)
+    return CudaPlan(blob=blob, const_payload=payload, const_bytes=const_bytes,
+                    image_bytes=image_bytes, placements=placements, index=index,
+                    n_ops=len(ops), op_names=tuple(op_names), inputs=tuple(graph.inputs),
+                    outputs=tuple(graph.outputs), skipped_reshapes=skipped,
+                    kinds=tuple(kinds))

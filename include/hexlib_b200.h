@@ -1,0 +1,242 @@
+/* include/hexlib_b200.h -- the C ABI of libhexlib_b200.so, the B200 (sm_100a)
+ * execution backend for hexlib's plan executor.
+ *
+ * Two groups of entry points, both plain C: pointers, sizes and an opaque
+ * stream handle, no C++ or torch types.
+ *
+ *  1. THE BATCH PATH. A session owns a CUDA stream and a set of device buffers
+ *     registered by `fd` (the analogue of the rpcmem fds the DSP maps), and runs
+ *     one hexlib batch blob -- the byte format of hexlib/runtime/wire.py:135-208
+ *     and hexlib/runtime/skel/hexlib_dsp.h:109-182, unchanged -- per `invoke`.
+ *     The first invoke of a blob validates it on the host, resolves every
+ *     (bi, offset) to a device address and captures all of its ops into one CUDA
+ *     graph; later invokes of the same blob replay that graph with one launch.
+ *     Lifecycle mirrors hexlib/runtime/idl/hexlib_iface.idl:28-67
+ *     (open/start -> mmap -> invoke -> munmap -> stop/close).
+ *
+ *  2. ONE FUNCTION PER KERNEL, with the argument list of that kernel's
+ *     kernels/<k>/kernel_api.h plus a trailing `void *stream` (a cudaStream_t,
+ *     NULL for the legacy default stream). Every pointer is a DEVICE pointer.
+ *     `hexlib_hf *` becomes `void *` (IEEE binary16 storage). The kernel_api.h
+ *     functions return void; these return a status, because a kernel that
+ *     cannot serve a request must say so (hexlib_dsp.h:197-199).
+ *
+ * STATUS CODES are hexlib_dsp.h's (:31-54) number for number: OK is 1, so a
+ * zero-filled response can never read as success. Codes this backend needs and
+ * the DSP did not are APPENDED (16, 17), never renumbered.
+ *
+ * THREADING. A session is single-threaded and `invoke` is not reentrant, the
+ * same contract as hexlib_dispatch_batch (skel_dispatch.c:134-147). Use one
+ * session per thread and one process per GPU.
+ */
+#ifndef HEXLIB_B200_H
+#define HEXLIB_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes: hexlib/runtime/skel/hexlib_dsp.h:31-54 ---------------- */
+#define HEXLIB_B200_OK                 1
+#define HEXLIB_B200_ERR_INTERNAL       2
+#define HEXLIB_B200_ERR_BAD_MAGIC      3
+#define HEXLIB_B200_ERR_BAD_VERSION    4
+#define HEXLIB_B200_ERR_TRUNCATED      5
+#define HEXLIB_B200_ERR_INVAL_PARAMS   6
+#define HEXLIB_B200_ERR_UNMAPPED       7
+#define HEXLIB_B200_ERR_NO_MMAP_SLOT   8
+#define HEXLIB_B200_ERR_MMAP_FAILED    9
+#define HEXLIB_B200_ERR_NO_KERNEL      10
+#define HEXLIB_B200_ERR_VTCM_TOO_SMALL 11
+#define HEXLIB_B200_ERR_VTCM_RECLAIMED 12
+#define HEXLIB_B200_ERR_REQUIRES       13
+#define HEXLIB_B200_ERR_NOT_STARTED    14
+#define HEXLIB_B200_ERR_CACHE          15
+/* Appended for this backend. */
+#define HEXLIB_B200_ERR_CUDA           16  /* a CUDA runtime call failed        */
+#define HEXLIB_B200_ERR_TIMEOUT        17  /* a device-side bounded wait expired */
+
+/* ---- wire constants: hexlib/runtime/wire.py:24-31, hexlib_dsp.h:23-30 ---- */
+#define HEXLIB_B200_BATCH_MAGIC   0x424C5848u  /* 'HXLB' */
+#define HEXLIB_B200_BATCH_VERSION 1u
+#define HEXLIB_B200_MAX_BUFS      8
+#define HEXLIB_B200_MAX_SRC       6
+#define HEXLIB_B200_MAX_DST       4
+#define HEXLIB_B200_MAX_PARAMS    16
+#define HEXLIB_B200_MAX_TENSORS   512
+
+/* Buffer flag (hexlib_buf_desc.flags, which the reference always writes 0):
+ * every tensor in a buffer carrying this flag is PER IMAGE. With n_images = B,
+ * such a tensor at per-image offset `o` of `nbytes` bytes occupies the B
+ * contiguous copies [B*o, B*o + B*nbytes) of the registered allocation, image
+ * b at B*o + b*nbytes -- so each kernel sees one contiguous [B, ...] array and
+ * a GEMM folds the images into its M dimension. With B = 1 the blob means
+ * exactly what it means to the DSP. */
+#define HEXLIB_B200_BUF_PER_IMAGE 1u
+
+/* Kernel ids on the wire: hexlib/runtime/genentry.py:67-88 (1..12 unchanged),
+ * then ids appended for kernels the DSP does not have. */
+#define HEXLIB_B200_KIND_ADD              1
+#define HEXLIB_B200_KIND_CAST             2
+#define HEXLIB_B200_KIND_LAYERNORM        3
+#define HEXLIB_B200_KIND_MATMUL           4
+#define HEXLIB_B200_KIND_MATMUL_EPILOGUE  5
+#define HEXLIB_B200_KIND_PATCHIFY         6
+#define HEXLIB_B200_KIND_RESHAPE          7
+#define HEXLIB_B200_KIND_ROPE_2D          8
+#define HEXLIB_B200_KIND_SCALE            9
+#define HEXLIB_B200_KIND_SOFTMAX          10
+#define HEXLIB_B200_KIND_TRANSPOSE        11  /* perm (1,0,2) */
+#define HEXLIB_B200_KIND_TRANSPOSE_HD     12  /* perm (0,2,1) */
+#define HEXLIB_B200_KIND_ATTENTION        13  /* scale->QK^T->softmax->PV, fused */
+#define HEXLIB_B200_KIND_RMSNORM          14
+#define HEXLIB_B200_KIND_MATMUL_EPILOGUE_RESIDUAL 15 /* act(a@w+b) + r */
+
+/* Invoke modes. */
+#define HEXLIB_B200_MODE_GRAPH   0u  /* capture once per blob, replay one graph  */
+#define HEXLIB_B200_MODE_EAGER   1u  /* launch op by op, time each with events   */
+
+#if defined(__GNUC__)
+#define HEXLIB_B200_API __attribute__((visibility("default")))
+#else
+#define HEXLIB_B200_API
+#endif
+
+typedef struct hexlib_b200_ctx hexlib_b200_ctx;
+
+/* ---- session: hexlib_iface.idl open/start (:32-35) and stop/close ------- */
+
+/* Open a session on CUDA device `device`: create its stream, load every
+ * kernel, and set their shared-memory limits, so nothing is loaded lazily
+ * inside a graph capture. */
+HEXLIB_B200_API int hexlib_b200_open(int device, hexlib_b200_ctx **out);
+/* Free every mapped buffer and cached graph, destroy the stream. */
+HEXLIB_B200_API int hexlib_b200_close(hexlib_b200_ctx *ctx);
+
+/* hexlib_iface.idl hwinfo (:59-60). Unlike the DSP's, every value is queried:
+ * arch is the device's compute capability as major*10+minor (100 on B200). */
+HEXLIB_B200_API int hexlib_b200_hwinfo(hexlib_b200_ctx *ctx, uint32_t *arch,
+                       uint32_t *sm_count, uint64_t *hbm_bytes,
+                       uint64_t *mapped_bytes);
+
+/* ---- buffers: hexlib_iface.idl mmap/munmap (:41-42) ---------------------- */
+
+/* Register buffer `fd` with `size` bytes, backed by one device allocation of
+ * size * replicas bytes (replicas >= 1; a per-image buffer needs one replica
+ * per image a later invoke names). Re-registering an fd is an error. */
+HEXLIB_B200_API int hexlib_b200_mmap(hexlib_b200_ctx *ctx, uint32_t fd, uint64_t size,
+                     uint32_t replicas);
+HEXLIB_B200_API int hexlib_b200_munmap(hexlib_b200_ctx *ctx, uint32_t fd);
+/* Host <-> device copies into a registered buffer at a BYTE offset of its
+ * allocation, ordered on the session stream and complete on return. */
+HEXLIB_B200_API int hexlib_b200_buf_write(hexlib_b200_ctx *ctx, uint32_t fd, uint64_t offset,
+                          const void *src, uint64_t nbytes);
+HEXLIB_B200_API int hexlib_b200_buf_read(hexlib_b200_ctx *ctx, uint32_t fd, uint64_t offset,
+                         void *dst, uint64_t nbytes);
+/* The device address of a buffer, for callers that hand it to NCCL/torch. */
+HEXLIB_B200_API int hexlib_b200_buf_device_ptr(hexlib_b200_ctx *ctx, uint32_t fd,
+                               uint64_t *ptr, uint64_t *alloc_bytes);
+/* The session's CUDA stream (a cudaStream_t). */
+HEXLIB_B200_API int hexlib_b200_stream(hexlib_b200_ctx *ctx, void **stream);
+
+/* ---- batch: hexlib_iface.idl invoke (:64-66) -> skel_dispatch.c:80 ------- */
+
+/* Run one batch blob on one image. Same response layout as the DSP:
+ * hexlib_batch_rsp_hdr then one hexlib_op_result per op that was reached.
+ * `cycles_total` and `results[i].cycles` carry NANOSECONDS of device time
+ * (CUDA events); per-op times are filled only in HEXLIB_B200_MODE_EAGER. */
+HEXLIB_B200_API int hexlib_b200_invoke(hexlib_b200_ctx *ctx, const uint8_t *batch,
+                       uint32_t len, uint8_t *rsp, uint32_t rsp_cap,
+                       uint32_t *rsp_len);
+/* The same for `n_images` images (see HEXLIB_B200_BUF_PER_IMAGE), in `mode`.
+ * If `sync` is 0 the call returns after enqueueing the work on the session
+ * stream (graph mode only); the response then reports only host validation
+ * and a later hexlib_b200_sync() reports device-side status. */
+HEXLIB_B200_API int hexlib_b200_invoke_images(hexlib_b200_ctx *ctx, const uint8_t *batch,
+                              uint32_t len, uint32_t n_images, uint32_t mode,
+                              uint32_t sync, uint8_t *rsp, uint32_t rsp_cap,
+                              uint32_t *rsp_len);
+/* Wait for the session stream; OK, ERR_CUDA or ERR_TIMEOUT. */
+HEXLIB_B200_API int hexlib_b200_sync(hexlib_b200_ctx *ctx);
+
+/* Host-only validation of a blob against buffer sizes, with no device and no
+ * session: the same checks invoke runs before its first launch, answered in
+ * the same response layout (each reached op OK or its error). buf_sizes[i] is
+ * the registered size of wire buffer i (in blob order). */
+HEXLIB_B200_API int hexlib_b200_check_batch(const uint8_t *batch, uint32_t len,
+                            const uint64_t *buf_sizes, uint32_t n_sizes,
+                            uint32_t n_images, uint8_t *rsp, uint32_t rsp_cap,
+                            uint32_t *rsp_len);
+
+/* The status as text (hexlib_dsp.h:71-91). */
+HEXLIB_B200_API const char *hexlib_b200_status_name(int status);
+
+/* ---- kernels: kernels/<k>/kernel_api.h + trailing stream ----------------- */
+
+/* kernels/add_fp16/kernel_api.h:35 */
+HEXLIB_B200_API int hexlib_b200_add_fp16(const void *a, const void *b, void *y, int n,
+                         void *stream);
+/* add with an fp32 right operand, rounded once: the pos_embed add of
+ * hexlib/models/vit.py:159-160 exactly as the numpy executor computes it. */
+HEXLIB_B200_API int hexlib_b200_add_fp16_f32(const void *a, const float *b, void *y, int n,
+                             void *stream);
+/* kernels/cast_f32_f16/kernel_api.h:33 */
+HEXLIB_B200_API int hexlib_b200_cast_f32_f16(const float *x, void *y, int n, void *stream);
+/* kernels/scale_fp16/kernel_api.h:37 */
+HEXLIB_B200_API int hexlib_b200_scale_fp16(const void *x, void *y, int n, float factor,
+                           void *stream);
+/* kernels/layernorm_fp16/kernel_api.h:38-39 */
+HEXLIB_B200_API int hexlib_b200_layernorm_fp16(const void *x, const float *w, const float *b,
+                               void *y, int R, int C, float eps, void *stream);
+/* kernels/rmsnorm_fp16/kernel_api.h:26-27 */
+HEXLIB_B200_API int hexlib_b200_rmsnorm_fp16(const void *x, const void *w, void *y, int R,
+                             int C, float eps, void *stream);
+/* kernels/softmax_fp16/kernel_api.h:69 */
+HEXLIB_B200_API int hexlib_b200_softmax_fp16(const void *x, void *y, int R, int C,
+                             void *stream);
+/* kernels/rope_2d_fp16/kernel_api.h:120-121 */
+HEXLIB_B200_API int hexlib_b200_rope_2d_fp16(const void *x, const float *costab,
+                             const float *sintab, void *y, int T, int H, int D,
+                             void *stream);
+/* kernels/transpose_th_fp16/kernel_api.h:38 */
+HEXLIB_B200_API int hexlib_b200_transpose_th_fp16(const void *x, void *y, int T, int H, int D,
+                                  void *stream);
+/* kernels/transpose_hd_fp16/kernel_api.h:67 */
+HEXLIB_B200_API int hexlib_b200_transpose_hd_fp16(const void *x, void *y, int B, int T, int D,
+                                  void *stream);
+/* kernels/patchify_fp32/kernel_api.h:116-118 */
+HEXLIB_B200_API int hexlib_b200_patchify_fp32(const float *img, float *out, int C, int T,
+                              int H, int W, int patch, int merge, int grid_h,
+                              int grid_w, void *stream);
+/* kernels/matmul_fp16/kernel_api.h:77-78 */
+HEXLIB_B200_API int hexlib_b200_matmul_fp16(const void *A, const void *B, void *C, int Bn,
+                            int M, int K, int N, void *stream);
+/* kernels/matmul_epilogue_fp16/kernel_api.h:188-190, with an fp16 [K, N]
+ * row-major weight in place of the q4_0 one; act is MM_ACT_* (0 none,
+ * 1 gelu_tanh, 2 gelu_erf, kernel_api.h:181-183). */
+HEXLIB_B200_API int hexlib_b200_matmul_epilogue_fp16(const void *a, const void *w,
+                                     const float *bias, void *out, int M,
+                                     int K, int N, int act, void *stream);
+/* matmul_epilogue followed by the residual add that consumes it
+ * (hexlib/models/vit.py:196 and :203): out = act(a@w + bias) + r, with the
+ * matmul result rounded to fp16 before the add, as the unfused plan does. */
+HEXLIB_B200_API int hexlib_b200_matmul_epilogue_residual_fp16(const void *a, const void *w,
+                                              const float *bias,
+                                              const void *r, void *out, int M,
+                                              int K, int N, int act,
+                                              void *stream);
+/* Fused attention over Bn independent heads, q/k/v/ctx [Bn, T, D] fp16:
+ * ctx = softmax((q*scale) @ k^T) @ v, the chain hexlib/models/vit.py:183-190
+ * writes as five ops, without materialising the [Bn, T, T] scores. */
+HEXLIB_B200_API int hexlib_b200_attention_fp16(const void *q, const void *k, const void *v,
+                               void *ctx, int Bn, int T, int D, float scale,
+                               void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HEXLIB_B200_H */

@@ -1,0 +1,102 @@
+"""The restated builder and fusion pass produce the reference's post-fusion
+graph, op for op, at every configuration the benchmark uses; the CUDA-only
+rewrites are checked for what they replace."""
+from __future__ import annotations
+
+import dataclasses
+import json
+import os
+from collections import Counter
+
+import pytest
+
+from hexlib_b200 import graph as G
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+PLANS = json.load(open(os.path.join(GOLDEN, "plans.json")))
+
+TINY16 = G.VitConfig(depth=2, hidden_size=64, num_heads=4, intermediate_size=128,
+                     patch_size=4, temporal_patch_size=2, in_channels=3,
+                     spatial_merge_size=2, out_hidden_size=32, layernorm_eps=1e-6,
+                     rope_theta=10000.0, image_size=32, act_dtype="fp16",
+                     weight_dtype="fp16")
+
+CONFIGS = {
+    "tiny_fp16": TINY16,
+    "qwen35_256": G.qwen35_at(256),
+    "qwen35_512": G.qwen35_at(512),
+    "qwen35_1024": G.qwen35_at(1024),
+}
+
+
+def _norm_attrs(a):
+    return {k: (list(v) if isinstance(v, tuple) else v) for k, v in dict(a).items()}
+
+
+@pytest.mark.parametrize("key", sorted(CONFIGS))
+def test_post_fusion_graph_equals_the_references(key):
+    ref = PLANS[key]
+    ep = G.compile_for_cuda(G.build_vision_encoder(CONFIGS[key]))
+    g = ep.graph
+    assert {n: [t.dtype, list(t.shape), t.const] for n, t in g.tensors.items()} == ref["tensors"]
+    mine = {o.id: [o.id, o.kind, list(o.inputs), list(o.outputs), _norm_attrs(o.attrs)]
+            for o in g.ops}
+    theirs = {o[0]: o for o in ref["ops"]}
+    assert mine == theirs
+    assert list(g.inputs) == ref["inputs"] and list(g.outputs) == ref["outputs"]
+    assert len(g.ops) == ref["n_steps"]
+
+
+def test_reference_plan_json_loads_in_plan_order():
+    text = open(os.path.join(GOLDEN, "tiny_compiled.json")).read()
+    ep = G.from_compiled_json(text)
+    assert [o.id for o in ep.graph.ops] == PLANS["tiny_fp16"]["step_order"]
+    assert [s.op.id for s in ep.plan.steps] == PLANS["tiny_fp16"]["step_order"]
+
+
+def test_encoder_op_census_at_256():
+    ep = G.compile_for_cuda(G.build_vision_encoder(G.qwen35_at(256)))
+    c = Counter(o.kind for o in ep.graph.ops)
+    assert c == Counter({"matmul_epilogue": 75, "transpose": 60, "reshape": 49, "add": 25,
+                         "layernorm": 25, "rope_2d": 24, "matmul": 24, "scale": 12,
+                         "softmax": 12, "patchify": 1, "cast": 1})
+
+
+def test_attention_rewrite_replaces_exactly_the_five_op_chain():
+    ep = G.compile_for_cuda(G.build_vision_encoder(G.qwen35_at(256)), attention=True)
+    c = Counter(o.kind for o in ep.graph.ops)
+    assert c["attention"] == 12
+    assert c["softmax"] == 0 and c["matmul"] == 0 and c["scale"] == 0
+    assert c["transpose"] == 48          # the perm (0,2,1) transposes are gone
+    for o in ep.graph.ops:
+        if o.kind == "attention":
+            assert o.attrs["scale"] == 0.125
+            assert all(ep.graph.tensors[n].shape == (12, 256, 64) for n in o.inputs)
+    assert not any(n.endswith(".scores") or n.endswith(".probs") for n in ep.graph.tensors)
+
+
+def test_residual_rewrite_folds_the_24_residual_adds():
+    ep = G.compile_for_cuda(G.build_vision_encoder(G.qwen35_at(256)), residual=True)
+    c = Counter(o.kind for o in ep.graph.ops)
+    assert c["matmul_epilogue_residual"] == 24
+    assert c["add"] == 1                 # only the pos_embed add remains
+    for o in ep.graph.ops:
+        if o.kind == "matmul_epilogue_residual":
+            assert o.attrs["act"] == "none"
+            assert not ep.graph.tensors[o.inputs[3]].const
+
+
+def test_rewrites_apply_to_a_reference_compiled_pair():
+    text = open(os.path.join(GOLDEN, "tiny_compiled.json")).read()
+    ep = G.from_compiled_json(text)
+    rw = G.rewrite_compiled(ep, attention=True, residual=True)
+    c = Counter(o.kind for o in rw.graph.ops)
+    assert c["attention"] == 2 and c["matmul_epilogue_residual"] == 4
+    assert rw.graph.problems() == []
+
+
+def test_invalid_configs_are_refused():
+    with pytest.raises(ValueError):
+        G.build_vision_encoder(dataclasses.replace(TINY16, image_size=30))
+    with pytest.raises(ValueError):
+        G.build_vision_encoder(dataclasses.replace(TINY16, num_heads=5))
