@@ -1,17 +1,398 @@
-// k_attention.cu -- fused attention (placeholder until the tcgen05 kernel
-// lands): refuses every call with ERR_NO_KERNEL, so the dispatcher reports the
-// op as unserved instead of computing anything.
+// k_attention.cu -- fused attention for the vision encoder on sm_100a:
+//   ctx = softmax((q * scale) @ k^T) @ v        per head, q/k/v/ctx [Bn, T, D]
+// which the plan writes as five ops per block (hexlib/models/vit.py:183-190:
+// scale, transpose_hd, matmul, softmax, matmul) and which, unfused, writes
+// and re-reads an [H, T, T] score and probability tensor per image and
+// layer. Here the scores live only in tensor memory and registers.
+//
+// TENSOR-CORE PATH (D = 64). One CTA owns 256 queries of one head as two
+// 128-row tiles (a and b) and streams the keys in blocks of 128:
+//   warp 0     TMA: both Q tiles once, then K and V blocks into a 3-stage ring;
+//   warp 1     one lane issues tcgen05.mma: S_t = Q_t K^T (M=128, N=128,
+//              K=64) into TMEM, and after the softmax has written P_t to shared
+//              memory, O_t = P_t V (M=128, N=64, K=128) into TMEM;
+//   warps 2-5  softmax of tile a, warps 6-9 softmax of tile b: one query row
+//              per thread, read from TMEM twice (row max, then exp2/sum/P),
+//              online rescaling of the running output held in registers.
+// While one tile's softmax runs, the tensor core works on the other tile's
+// products, so the exp units and the tensor core overlap.
+//
+// NUMERICS. S and O accumulate in fp32; the running max, exp2 and row sums
+// are fp32; P is rounded to fp16 for its MMA (unnormalised, in [0, 1]) and
+// the output is divided by the fp32 row sum and rounded to fp16 once. The
+// unfused plan instead rounds the scores and the normalised probabilities to
+// fp16; the two agree within the fp16 per-op tolerance.
+//
+// Any other D uses a CUDA-core kernel with the same online softmax.
+#include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
+#include <stdint.h>
 
+#include "hb_device.cuh"
 #include "hb_kernels.h"
+#include "hb_tma.h"
 
 namespace hb {
+namespace {
 
-int attention_kernels_init() { return HEXLIB_B200_OK; }
+constexpr int AT_BM = 128;      // query rows per tile
+constexpr int AT_BN = 128;      // keys per block
+constexpr int AT_D = 64;
+constexpr int AT_STAGES = 3;
+constexpr int AT_THREADS = 320;
+constexpr int AT_TILE = AT_BM * AT_D * 2;        // 16 KiB: one Q, K or V tile
+constexpr int AT_P = AT_BM * AT_BN * 2;          // 32 KiB: P as two 64-key atoms
+constexpr int AT_SMEM = 2 * AT_TILE + AT_STAGES * 2 * AT_TILE + 2 * AT_P + 1024 + 256;
+constexpr uint32_t AT_TMEM_COLS = 512;           // S_a, S_b: 128 each; O_a, O_b: 64 each
 
-int launch_attention(const void*, const void*, const void*, void*, int64_t,
-                     int, int, float, int*, cudaStream_t) {
-  return HEXLIB_B200_ERR_NO_KERNEL;
+struct AttnParams {
+  int T;
+  int64_t Bn;
+  int q_pairs;        // ceil(T / 256)
+  float c_log2;       // scale * log2(e)
+  __half* out;
+  int* err;
+};
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(AT_THREADS, 1)
+    attention_tc(const __grid_constant__ CUtensorMap tmQ,
+                 const __grid_constant__ CUtensorMap tmK,
+                 const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                                  // [2][16 KiB]
+  uint8_t* sK = sQ + 2 * AT_TILE;                      // [STAGES][16 KiB]
+  uint8_t* sV = sK + AT_STAGES * AT_TILE;              // [STAGES][16 KiB]
+  uint8_t* sP = sV + AT_STAGES * AT_TILE;              // [2][32 KiB]
+  uint64_t* q_full = reinterpret_cast<uint64_t*>(sP + 2 * AT_P);
+  uint64_t* kv_full = q_full + 1;
+  uint64_t* kv_empty = kv_full + AT_STAGES;
+  uint64_t* s_full = kv_empty + AT_STAGES;   // [2]
+  uint64_t* s_free = s_full + 2;             // [2]
+  uint64_t* p_full = s_free + 2;             // [2]
+  uint64_t* o_full = p_full + 2;             // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t bn = blockIdx.x / p.q_pairs;
+  const int q0 = (int)(blockIdx.x % p.q_pairs) * (2 * AT_BM);
+  const int nkv = (p.T + AT_BN - 1) / AT_BN;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < AT_STAGES; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&s_free[t], 4);
+      mbar_init(&p_full[t], 4);
+      mbar_init(&o_full[t], 1);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, AT_TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, 2 * AT_TILE);
+      tma_load_3d(&tmQ, q_full, sQ, 0, q0, (int)bn);
+      tma_load_3d(&tmQ, q_full, sQ + AT_TILE, 0, q0 + AT_BM, (int)bn);
+      for (int j = 0; j < nkv; ++j) {
+        const int st = j % AT_STAGES;
+        const uint32_t ph = (uint32_t)(j / AT_STAGES) & 1u;
+        if (!mbar_wait(&kv_empty[st], ph ^ 1u, abort_flag, p.err)) goto done;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * AT_TILE);
+        tma_load_3d(&tmK, &kv_full[st], sK + st * AT_TILE, 0, j * AT_BN, (int)bn);
+        tma_load_3d(&tmV, &kv_full[st], sV + st * AT_TILE, 0, j * AT_BN, (int)bn);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_f16_f32(AT_BM, AT_BN, false, false);
+      constexpr uint32_t idesc_o = idesc_f16_f32(AT_BM, AT_D, false, true);
+      if (!mbar_wait(q_full, 0, abort_flag, p.err)) goto done;
+      // S_t(j) = Q_t K_j^T
+      auto issue_s = [&](int t, int j) -> bool {
+        const int st = j % AT_STAGES;
+        if (!mbar_wait(&kv_full[st], (uint32_t)(j / AT_STAGES) & 1u, abort_flag, p.err))
+          return false;
+        if (j > 0 && !mbar_wait(&s_free[t], (uint32_t)(j - 1) & 1u, abort_flag, p.err))
+          return false;
+        tc_fence_after();
+        const uint32_t qa = smem_u32(sQ + t * AT_TILE);
+        const uint32_t kb = smem_u32(sK + st * AT_TILE);
+#pragma unroll
+        for (int kk = 0; kk < AT_D / 16; ++kk)
+          umma_f16(tmem + (uint32_t)(t * AT_BN), sdesc_sw128(qa + kk * 32, 16, 1024),
+                   sdesc_sw128(kb + kk * 32, 16, 1024), idesc_s, kk ? 1u : 0u);
+        umma_commit(&s_full[t]);
+        return true;
+      };
+      // O_t(j) = P_t(j) V_j
+      auto issue_pv = [&](int t, int j) -> bool {
+        const int st = j % AT_STAGES;
+        if (!mbar_wait(&p_full[t], (uint32_t)j & 1u, abort_flag, p.err)) return false;
+        tc_fence_after();
+        const uint32_t pa = smem_u32(sP + t * AT_P);
+        const uint32_t vb = smem_u32(sV + st * AT_TILE);
+#pragma unroll
+        for (int kk = 0; kk < AT_BN / 16; ++kk)
+          umma_f16(tmem + 256u + (uint32_t)(t * AT_D),
+                   sdesc_sw128(pa + (kk >> 2) * (AT_BM * 128) + (kk & 3) * 32, 16, 1024),
+                   sdesc_sw128(vb + kk * 2048, 8192, 1024), idesc_o, kk ? 1u : 0u);
+        umma_commit(&o_full[t]);
+        return true;
+      };
+      if (!issue_s(0, 0) || !issue_s(1, 0)) goto done;
+      for (int j = 0; j < nkv; ++j) {
+        if (!issue_pv(0, j)) goto done;
+        if (j + 1 < nkv && !issue_s(0, j + 1)) goto done;
+        if (!issue_pv(1, j)) goto done;
+        umma_commit(&kv_empty[j % AT_STAGES]);   // K_j and V_j fully consumed
+        if (j + 1 < nkv && !issue_s(1, j + 1)) goto done;
+      }
+    }
+  } else {
+    // softmax warpgroups: t = 0 (warps 2-5) or 1 (warps 6-9)
+    const int t = (warp - 2) >> 2;
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;               // row within the tile
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t s_col = tmem + lane_off + (uint32_t)(t * AT_BN);
+    const uint32_t o_col = tmem + lane_off + 256u + (uint32_t)(t * AT_D);
+    uint8_t* prow = sP + t * AT_P + r * 128;
+    const float c = p.c_log2;
+    float m_run = -INFINITY, l_run = 0.f, alpha_prev = 1.f;
+    float o[AT_D];
+#pragma unroll
+    for (int i = 0; i < AT_D; ++i) o[i] = 0.f;
+
+    for (int j = 0; j < nkv; ++j) {
+      const bool ok = mbar_wait(&s_full[t], (uint32_t)j & 1u, abort_flag, p.err);
+      if (!__all_sync(0xffffffffu, ok)) goto done;
+      tc_fence_after();
+      const int key0 = j * AT_BN;
+      // pass 1: row max of the scaled scores
+      float mx = -INFINITY;
+#pragma unroll
+      for (int cc = 0; cc < AT_BN / 32; ++cc) {
+        uint32_t rg[32];
+        tmem_ld_32x32b_x32(s_col + cc * 32, rg);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float v = (key0 + cc * 32 + i < p.T) ? __uint_as_float(rg[i]) * c : -INFINITY;
+          mx = fmaxf(mx, v);
+        }
+      }
+      const float m_new = fmaxf(m_run, mx);
+      const float alpha = exp2f(m_run - m_new);
+      // fold the previous block's P V into the running output
+      if (j > 0) {
+        const bool ok2 = mbar_wait(&o_full[t], (uint32_t)(j - 1) & 1u, abort_flag, p.err);
+        if (!__all_sync(0xffffffffu, ok2)) goto done;
+        tc_fence_after();
+#pragma unroll
+        for (int h = 0; h < AT_D / 32; ++h) {
+          uint32_t rg[32];
+          tmem_ld_32x32b_x32(o_col + h * 32, rg);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            o[h * 32 + i] = o[h * 32 + i] * alpha_prev + __uint_as_float(rg[i]);
+        }
+      }
+      // pass 2: p = exp2(s*c - m), row sum, P to shared memory (swizzled)
+      float rs = 0.f;
+#pragma unroll
+      for (int cc = 0; cc < AT_BN / 32; ++cc) {
+        uint32_t rg[32];
+        tmem_ld_32x32b_x32(s_col + cc * 32, rg);
+        tmem_ld_wait();
+        uint32_t h2[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int k0 = key0 + cc * 32 + 2 * i;
+          const float p0 = (k0 < p.T) ? exp2f(__uint_as_float(rg[2 * i]) * c - m_new) : 0.f;
+          const float p1 = (k0 + 1 < p.T) ? exp2f(__uint_as_float(rg[2 * i + 1]) * c - m_new) : 0.f;
+          rs += p0 + p1;
+          h2[i] = pack_half2(p0, p1);
+        }
+        uint8_t* atom = prow + (cc >> 1) * (AT_BM * 128);
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const int chunk = ((cc & 1) * 4 + g) ^ (r & 7);
+          *reinterpret_cast<uint4*>(atom + chunk * 16) =
+              make_uint4(h2[4 * g], h2[4 * g + 1], h2[4 * g + 2], h2[4 * g + 3]);
+        }
+      }
+      tc_fence_before();
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&s_free[t]);
+        mbar_arrive(&p_full[t]);
+      }
+      l_run = l_run * alpha + rs;
+      m_run = m_new;
+      alpha_prev = alpha;
+    }
+    {
+      const bool ok = mbar_wait(&o_full[t], (uint32_t)(nkv - 1) & 1u, abort_flag, p.err);
+      if (!__all_sync(0xffffffffu, ok)) goto done;
+      tc_fence_after();
+#pragma unroll
+      for (int h = 0; h < AT_D / 32; ++h) {
+        uint32_t rg[32];
+        tmem_ld_32x32b_x32(o_col + h * 32, rg);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          o[h * 32 + i] = o[h * 32 + i] * alpha_prev + __uint_as_float(rg[i]);
+      }
+      const int row = q0 + t * AT_BM + r;
+      if (row < p.T) {
+        const float inv = 1.0f / l_run;
+        uint4* dst = reinterpret_cast<uint4*>(p.out + (bn * p.T + row) * (int64_t)AT_D);
+#pragma unroll
+        for (int g = 0; g < AT_D / 8; ++g)
+          dst[g] = make_uint4(pack_half2(o[8 * g] * inv, o[8 * g + 1] * inv),
+                              pack_half2(o[8 * g + 2] * inv, o[8 * g + 3] * inv),
+                              pack_half2(o[8 * g + 4] * inv, o[8 * g + 5] * inv),
+                              pack_half2(o[8 * g + 6] * inv, o[8 * g + 7] * inv));
+      }
+    }
+  }
+
+done:
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, AT_TMEM_COLS);
+  }
+}
+
+// CUDA-core fallback: one thread per query row, online softmax, D <= 256.
+template <int DMAX>
+__global__ void attention_simt(const __half* __restrict__ q, const __half* __restrict__ k,
+                               const __half* __restrict__ v, __half* __restrict__ out,
+                               int64_t Bn, int T, int D, float scale) {
+  const int64_t rows = Bn * T;
+  for (int64_t rr = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; rr < rows;
+       rr += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t b = rr / T;
+    const __half* qr = q + rr * D;
+    const __half* kb = k + b * (int64_t)T * D;
+    const __half* vb = v + b * (int64_t)T * D;
+    float qf[DMAX], o[DMAX];
+    for (int d = 0; d < D; ++d) {
+      qf[d] = __half2float(qr[d]);
+      o[d] = 0.f;
+    }
+    float m = -INFINITY, l = 0.f;
+    for (int j = 0; j < T; ++j) {
+      float s = 0.f;
+      for (int d = 0; d < D; ++d) s += qf[d] * __half2float(kb[(int64_t)j * D + d]);
+      s *= scale;
+      const float mn = fmaxf(m, s);
+      const float a = expf(m - mn);
+      const float pj = expf(s - mn);
+      l = l * a + pj;
+      for (int d = 0; d < D; ++d) o[d] = o[d] * a + pj * __half2float(vb[(int64_t)j * D + d]);
+      m = mn;
+    }
+    for (int d = 0; d < D; ++d) out[rr * D + d] = __float2half_rn(o[d] / l);
+  }
+}
+
+bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+int g_sms = 0;
+
+}  // namespace
+
+int attention_kernels_init() {
+  if (cudaFuncSetAttribute(attention_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           AT_SMEM) != cudaSuccess) {
+    cudaGetLastError();
+    return HEXLIB_B200_ERR_CUDA;
+  }
+  cudaFuncAttributes a;
+  if (cudaFuncGetAttributes(&a, attention_simt<256>) != cudaSuccess) {
+    cudaGetLastError();
+    return HEXLIB_B200_ERR_CUDA;
+  }
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev);
+  if (g_sms <= 0) g_sms = 148;
+  return HEXLIB_B200_OK;
+}
+
+int launch_attention(const void* q, const void* k, const void* v, void* ctx, int64_t Bn,
+                     int T, int D, float scale, int* err, cudaStream_t s) {
+  if (Bn < 0 || T <= 0 || D <= 0 || D > 256) return HEXLIB_B200_ERR_INVAL_PARAMS;
+  if (Bn == 0) return HEXLIB_B200_OK;
+  if (!q || !k || !v || !ctx) return HEXLIB_B200_ERR_INVAL_PARAMS;
+  if (D == AT_D && aligned16(q) && aligned16(k) && aligned16(v) && aligned16(ctx) &&
+      Bn < (int64_t)1 << 30 && tma_available()) {
+    CUtensorMap mq, mk, mv;
+    const bool ok = make_tmap_3d_f16(&mq, q, AT_D, (uint64_t)T, (uint64_t)Bn, 64, AT_BM) &&
+                    make_tmap_3d_f16(&mk, k, AT_D, (uint64_t)T, (uint64_t)Bn, 64, AT_BN) &&
+                    make_tmap_3d_f16(&mv, v, AT_D, (uint64_t)T, (uint64_t)Bn, 64, AT_BN);
+    if (ok) {
+      AttnParams p;
+      p.T = T;
+      p.Bn = Bn;
+      p.q_pairs = (T + 2 * AT_BM - 1) / (2 * AT_BM);
+      p.c_log2 = scale * 1.4426950408889634f;
+      p.out = reinterpret_cast<__half*>(ctx);
+      p.err = err;
+      const int64_t grid = Bn * p.q_pairs;
+      attention_tc<<<(unsigned)grid, AT_THREADS, AT_SMEM, s>>>(mq, mk, mv, p);
+      if (cudaPeekAtLastError() != cudaSuccess) {
+        cudaGetLastError();
+        return HEXLIB_B200_ERR_CUDA;
+      }
+      return HEXLIB_B200_OK;
+    }
+  }
+  const int64_t rows = Bn * T;
+  int64_t blocks = (rows + 127) / 128;
+  const int64_t cap = (int64_t)(g_sms > 0 ? g_sms : 148) * 8;
+  if (blocks > cap) blocks = cap;
+  attention_simt<256><<<(unsigned)blocks, 128, 0, s>>>(
+      reinterpret_cast<const __half*>(q), reinterpret_cast<const __half*>(k),
+      reinterpret_cast<const __half*>(v), reinterpret_cast<__half*>(ctx), Bn, T, D, scale);
+  if (cudaPeekAtLastError() != cudaSuccess) {
+    cudaGetLastError();
+    return HEXLIB_B200_ERR_CUDA;
+  }
+  return HEXLIB_B200_OK;
 }
 
 }  // namespace hb
