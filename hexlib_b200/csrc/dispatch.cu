@@ -1134,6 +1134,14 @@ int hexlib_b200_invoke_images(hexlib_b200_ctx* ctx, const uint8_t* batch,
   return status;
 }
 
+int hexlib_b200_diag_wait_timeout(hexlib_b200_ctx* ctx, uint32_t limit_us) {
+  if (!ctx) return HEXLIB_B200_ERR_NOT_STARTED;
+  cudaSetDevice(ctx->device);
+  const int rc = hb::launch_wait_timeout_probe(ctx->err_dev, limit_us, ctx->stream);
+  if (rc != HEXLIB_B200_OK) return rc;
+  return hexlib_b200_sync(ctx);
+}
+
 int hexlib_b200_invoke(hexlib_b200_ctx* ctx, const uint8_t* batch, uint32_t len,
                        uint8_t* rsp, uint32_t rsp_cap, uint32_t* rsp_len) {
   return hexlib_b200_invoke_images(ctx, batch, len, 1, HEXLIB_B200_MODE_GRAPH,

@@ -15,6 +15,7 @@ namespace hb {
 int memory_kernels_init();
 int gemm_kernels_init();
 int attention_kernels_init();
+int diag_kernels_init();
 
 namespace {
 std::once_flag g_init_once;
@@ -27,6 +28,7 @@ int kernels_init() {
     int rc = memory_kernels_init();
     if (rc == HEXLIB_B200_OK) rc = gemm_kernels_init();
     if (rc == HEXLIB_B200_OK) rc = attention_kernels_init();
+    if (rc == HEXLIB_B200_OK) rc = diag_kernels_init();
     int* host = nullptr;
     if (rc == HEXLIB_B200_OK &&
         cudaHostAlloc(reinterpret_cast<void**>(&host), sizeof(int),

@@ -70,12 +70,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Wait for the phase with `parity` to complete. Returns false if the shared
-// abort flag was raised by another role or the time limit passed; in the
-// latter case the first thread to notice raises the abort flag and records
-// the error, so every other role stops at its next wait.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          volatile int* abort_flag,
-                                          int* err) {
+// abort flag was raised by another role or `limit_ns` passed; in the latter
+// case the first thread to notice raises the abort flag and records the
+// error, so every other role stops at its next wait.
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity,
+                                                volatile int* abort_flag,
+                                                int* err, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   uint32_t n = 0;
@@ -83,13 +83,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
     if (mbar_try_wait(bar, parity)) return true;
     if ((++n & 63u) == 0) {
       if (*abort_flag) return false;
-      if (global_timer_ns() - t0 > HB_WAIT_LIMIT_NS) {
+      if (global_timer_ns() - t0 > limit_ns) {
         *abort_flag = 1;
         if (err) atomicExch(err, HB_DEVERR_WAIT_TIMEOUT);
         return false;
       }
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          volatile int* abort_flag,
+                                          int* err) {
+  return mbar_wait_limit(bar, parity, abort_flag, err, HB_WAIT_LIMIT_NS);
 }
 
 // ---- TMA (no multicast anywhere in this project) ---------------------------
@@ -106,6 +112,31 @@ __device__ __forceinline__ void tma_load_3d(const CUtensorMap* map,
       "bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(smem_dst)),
       "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
+}
+
+// Bulk tensor store shared::cta -> global, tracked by bulk async-groups.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map,
+                                             const void* smem_src, int c0,
+                                             int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, "
+      "%4}], [%1];" ::"l"(map),
+      "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Wait until every committed bulk store has finished READING shared memory.
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Wait until every committed bulk store has completed.
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // ---- tcgen05 ---------------------------------------------------------------
@@ -249,7 +280,7 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(uint32_t M, uint32_t N,
 __device__ __forceinline__ float gelu_tanh_f(float x) {
   const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
   const float u = k0 * (x + 0.044715f * x * x * x);
-  return x / (1.0f + __expf(-2.0f * u));
+  return __fdividef(x, 1.0f + __expf(-2.0f * u));
 }
 
 // GELU, exact erf form (elementwise.py:117-125).

@@ -72,6 +72,10 @@ int launch_attention(const void* q, const void* k, const void* v, void* ctx,
                      int64_t Bn, int T, int D, float scale, int* err,
                      cudaStream_t s);
 
+// Diagnostic: a kernel whose bounded wait never completes; it records a
+// timeout in `err` after `limit_us` and returns.
+int launch_wait_timeout_probe(int* err, uint32_t limit_us, cudaStream_t s);
+
 // One-time per-process setup of kernel attributes (dynamic shared memory
 // limits); safe to call repeatedly. Returns a status.
 int kernels_init();

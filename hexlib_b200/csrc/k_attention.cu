@@ -55,6 +55,15 @@ struct AttnParams {
   int* err;
 };
 
+// 2^x with the hardware's approximate exponential (one MUFU.EX2): the
+// softmax feeds it arguments <= 0 and keeps its results in fp32 before they
+// are rounded to fp16.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -195,60 +204,78 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       if (!__all_sync(0xffffffffu, ok)) goto done;
       tc_fence_after();
       const int key0 = j * AT_BN;
-      // pass 1: row max of the scaled scores
-      float mx = -INFINITY;
+      const int valid = p.T - key0;          // keys of this block that exist
+      // pass 1: row max of the raw scores, two 32-column chunks per TMEM
+      // round trip and eight independent partial maxima
+      float pm[8];
 #pragma unroll
-      for (int cc = 0; cc < AT_BN / 32; ++cc) {
-        uint32_t rg[32];
-        tmem_ld_32x32b_x32(s_col + cc * 32, rg);
+      for (int i = 0; i < 8; ++i) pm[i] = -INFINITY;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t ra[32], rb[32];
+        tmem_ld_32x32b_x32(s_col + half * 64, ra);
+        tmem_ld_32x32b_x32(s_col + half * 64 + 32, rb);
         tmem_ld_wait();
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const float v = (key0 + cc * 32 + i < p.T) ? __uint_as_float(rg[i]) * c : -INFINITY;
-          mx = fmaxf(mx, v);
+          const int ka = half * 64 + i, kb = half * 64 + 32 + i;
+          pm[i & 7] = fmaxf(pm[i & 7], ka < valid ? __uint_as_float(ra[i]) : -INFINITY);
+          pm[i & 7] = fmaxf(pm[i & 7], kb < valid ? __uint_as_float(rb[i]) : -INFINITY);
         }
       }
-      const float m_new = fmaxf(m_run, mx);
-      const float alpha = exp2f(m_run - m_new);
+      const float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
+                             fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
+      // the scale is positive, so max(s)*c is the max of s*c
+      const float m_new = fmaxf(m_run, mx * c);
+      const float alpha = ex2_approx(m_run - m_new);
       // fold the previous block's P V into the running output
       if (j > 0) {
         const bool ok2 = mbar_wait(&o_full[t], (uint32_t)(j - 1) & 1u, abort_flag, p.err);
         if (!__all_sync(0xffffffffu, ok2)) goto done;
         tc_fence_after();
+        uint32_t ra[32], rb[32];
+        tmem_ld_32x32b_x32(o_col, ra);
+        tmem_ld_32x32b_x32(o_col + 32, rb);
+        tmem_ld_wait();
 #pragma unroll
-        for (int h = 0; h < AT_D / 32; ++h) {
-          uint32_t rg[32];
-          tmem_ld_32x32b_x32(o_col + h * 32, rg);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            o[h * 32 + i] = o[h * 32 + i] * alpha_prev + __uint_as_float(rg[i]);
+        for (int i = 0; i < 32; ++i) {
+          o[i] = fmaf(o[i], alpha_prev, __uint_as_float(ra[i]));
+          o[32 + i] = fmaf(o[32 + i], alpha_prev, __uint_as_float(rb[i]));
         }
       }
-      // pass 2: p = exp2(s*c - m), row sum, P to shared memory (swizzled)
-      float rs = 0.f;
+      // pass 2: p = 2^(s*c - m), eight partial row sums, P to shared memory
+      float ps[8];
 #pragma unroll
-      for (int cc = 0; cc < AT_BN / 32; ++cc) {
-        uint32_t rg[32];
-        tmem_ld_32x32b_x32(s_col + cc * 32, rg);
+      for (int i = 0; i < 8; ++i) ps[i] = 0.f;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t ra[32], rb[32];
+        tmem_ld_32x32b_x32(s_col + half * 64, ra);
+        tmem_ld_32x32b_x32(s_col + half * 64 + 32, rb);
         tmem_ld_wait();
-        uint32_t h2[16];
+        uint32_t h2[32];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const int k0 = key0 + cc * 32 + 2 * i;
-          const float p0 = (k0 < p.T) ? exp2f(__uint_as_float(rg[2 * i]) * c - m_new) : 0.f;
-          const float p1 = (k0 + 1 < p.T) ? exp2f(__uint_as_float(rg[2 * i + 1]) * c - m_new) : 0.f;
-          rs += p0 + p1;
+          const int k0 = half * 64 + 2 * i;
+          const float p0 = k0 < valid ? ex2_approx(fmaf(__uint_as_float(ra[2 * i]), c, -m_new)) : 0.f;
+          const float p1 = k0 + 1 < valid ? ex2_approx(fmaf(__uint_as_float(ra[2 * i + 1]), c, -m_new)) : 0.f;
+          const float p2 = k0 + 32 < valid ? ex2_approx(fmaf(__uint_as_float(rb[2 * i]), c, -m_new)) : 0.f;
+          const float p3 = k0 + 33 < valid ? ex2_approx(fmaf(__uint_as_float(rb[2 * i + 1]), c, -m_new)) : 0.f;
+          ps[(2 * i) & 7] += p0 + p2;
+          ps[(2 * i + 1) & 7] += p1 + p3;
           h2[i] = pack_half2(p0, p1);
+          h2[16 + i] = pack_half2(p2, p3);
         }
-        uint8_t* atom = prow + (cc >> 1) * (AT_BM * 128);
+        // keys [half*64, half*64 + 64) are exactly one 128-byte atom row
+        uint8_t* atom = prow + half * (AT_BM * 128);
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          const int chunk = ((cc & 1) * 4 + g) ^ (r & 7);
+        for (int g = 0; g < 8; ++g) {
+          const int chunk = g ^ (r & 7);
           *reinterpret_cast<uint4*>(atom + chunk * 16) =
               make_uint4(h2[4 * g], h2[4 * g + 1], h2[4 * g + 2], h2[4 * g + 3]);
         }
       }
+      const float rs = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
       tc_fence_before();
       fence_proxy_async_smem();
       __syncwarp();
@@ -271,7 +298,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         tmem_ld_wait();
 #pragma unroll
         for (int i = 0; i < 32; ++i)
-          o[h * 32 + i] = o[h * 32 + i] * alpha_prev + __uint_as_float(rg[i]);
+          o[h * 32 + i] = fmaf(o[h * 32 + i], alpha_prev, __uint_as_float(rg[i]));
       }
       const int row = q0 + t * AT_BM + r;
       if (row < p.T) {
@@ -358,8 +385,10 @@ int launch_attention(const void* q, const void* k, const void* v, void* ctx, int
   if (Bn < 0 || T <= 0 || D <= 0 || D > 256) return HEXLIB_B200_ERR_INVAL_PARAMS;
   if (Bn == 0) return HEXLIB_B200_OK;
   if (!q || !k || !v || !ctx) return HEXLIB_B200_ERR_INVAL_PARAMS;
-  if (D == AT_D && aligned16(q) && aligned16(k) && aligned16(v) && aligned16(ctx) &&
-      Bn < (int64_t)1 << 30 && tma_available()) {
+  // The tensor-core kernel takes the row max of the raw scores and scales it,
+  // which is the max of the scaled scores only for a positive scale.
+  if (D == AT_D && scale > 0.f && aligned16(q) && aligned16(k) && aligned16(v) &&
+      aligned16(ctx) && Bn < (int64_t)1 << 30 && tma_available()) {
     CUtensorMap mq, mk, mv;
     const bool ok = make_tmap_3d_f16(&mq, q, AT_D, (uint64_t)T, (uint64_t)Bn, 64, AT_BM) &&
                     make_tmap_3d_f16(&mk, k, AT_D, (uint64_t)T, (uint64_t)Bn, 64, AT_BN) &&

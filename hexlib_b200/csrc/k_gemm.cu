@@ -52,7 +52,8 @@ struct GemmCfg {
   static constexpr int B_BYTES = BN * BK * 2;   // BN/64 boxes of 8 KiB
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;      // two fp32 accumulators
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int STAGING = kEpiWarps * 4096;  // one 32x64 fp16 box per warp
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGING + 1024 + 256;
 };
 
 struct GemmParams {
@@ -73,14 +74,16 @@ struct GemmParams {
 template <int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_f16_tc(const __grid_constant__ CUtensorMap tmA,
-                const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
+                const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
   using Cfg = GemmCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + Cfg::STAGES * Cfg::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + Cfg::STAGES * Cfg::B_BYTES);
+  uint8_t* sOut = sB + Cfg::STAGES * Cfg::B_BYTES;   // [kEpiWarps][4 KiB]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + Cfg::STAGING);
   uint64_t* empty = full + Cfg::STAGES;
   uint64_t* tfull = empty + Cfg::STAGES;
   uint64_t* tempty = tfull + 2;
@@ -105,6 +108,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
@@ -183,10 +187,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
+    // Epilogue. Warp (quarter, colhalf) owns TMEM lanes [32q, 32q+32) -- rows
+    // of the tile -- and half of its columns, in groups of 64: each group is
+    // read from TMEM 32 columns at a time, finished in registers (bias, GELU,
+    // residual, rounding), written to this warp's 128B-swizzled staging box
+    // and stored to global memory by one TMA store, which also clips the
+    // tile's row and column tails.
     const int ew = warp - 2;
-    const int quarter = warp & 3;  // TMEM lanes this warp may access
+    const int quarter = warp & 3;
     const int colhalf = ew >> 2;
-    constexpr int kChunks = BN / 32;
+    constexpr int kGroups = BN / 64;                          // 64-column groups
+    const int g_lo = (kGroups >= 2) ? colhalf * (kGroups / 2) : 0;
+    const int g_hi = (kGroups >= 2) ? (colhalf + 1) * (kGroups / 2) : (colhalf ? 0 : 1);
+    uint8_t* stage = sOut + ew * 4096;
+    const int rl = lane;                                      // row within the slab
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int64_t t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
@@ -203,33 +217,44 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const bool row_ok = row < p.M;
       const uint32_t trow =
           tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
-      __half* orow = p.out + (b * p.M + row) * (int64_t)p.N;
       const __half* rrow =
-          p.resid ? p.resid + (b * p.M + row) * (int64_t)p.N : nullptr;
+          (p.resid && row_ok) ? p.resid + (b * p.M + row) * (int64_t)p.N : nullptr;
 #pragma unroll 1
-      for (int c = colhalf * (kChunks / 2); c < (colhalf + 1) * (kChunks / 2);
-           ++c) {
-        uint32_t rg[32];
-        tmem_ld_32x32b_x32(trow + c * 32, rg);
-        tmem_ld_wait();
-        const int n0 = nb * BN + c * 32;
-        if (row_ok && n0 < p.N) {
-          float v[32];
+      for (int g = g_lo; g < g_hi; ++g) {
+        // the previous group's store must have finished reading the stage
+        if (lane == 0) bulk_wait_read_all();
+        __syncwarp();
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(rg[j]);
-          if (p.bias) {
+        for (int h = 0; h < 2; ++h) {
+          const int c32 = g * 64 + h * 32;          // column within the tile
+          const int n0 = nb * BN + c32;             // global column
+          // issue the global loads first so their latency overlaps the TMEM read
+          float bias[32];
+          if (p.bias && n0 < p.N) {
             const float4* bp = reinterpret_cast<const float4*>(p.bias + n0);
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-              if (n0 + 4 * j < p.N) {
-                const float4 bb = __ldg(bp + j);
-                v[4 * j] += bb.x;
-                v[4 * j + 1] += bb.y;
-                v[4 * j + 2] += bb.z;
-                v[4 * j + 3] += bb.w;
-              }
+              const float4 bb = (n0 + 4 * j < p.N) ? __ldg(bp + j) : make_float4(0, 0, 0, 0);
+              bias[4 * j] = bb.x; bias[4 * j + 1] = bb.y;
+              bias[4 * j + 2] = bb.z; bias[4 * j + 3] = bb.w;
             }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) bias[j] = 0.f;
           }
+          uint4 res[4];
+          if (rrow) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              res[j] = (n0 + 8 * j < p.N) ? __ldg(reinterpret_cast<const uint4*>(rrow + n0) + j)
+                                          : make_uint4(0, 0, 0, 0);
+          }
+          uint32_t rg[32];
+          tmem_ld_32x32b_x32(trow + c32, rg);
+          tmem_ld_wait();
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(rg[j]) + bias[j];
           if (p.act == 1) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = gelu_tanh_f(v[j]);
@@ -237,31 +262,38 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = gelu_erf_f(v[j]);
           }
+          uint32_t hw[16];
+          if (rrow) {
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            if (n0 + 8 * g >= p.N) break;
-            uint4 o;
-            uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
-            if (rrow) {
-              const uint4 rv = __ldg(reinterpret_cast<const uint4*>(rrow + n0) + g);
-              const __half2* rh = reinterpret_cast<const __half2*>(&rv);
+            for (int j = 0; j < 4; ++j) {
+              const __half2* rh = reinterpret_cast<const __half2*>(&res[j]);
 #pragma unroll
               for (int q = 0; q < 4; ++q) {
                 // The matmul result is an fp16 tensor in the unfused plan:
                 // round it, then add the residual in fp32 and round again.
-                const __half2 mm = __floats2half2_rn(v[8 * g + 2 * q],
-                                                     v[8 * g + 2 * q + 1]);
-                const float2 fm = __half22float2(mm);
+                const float2 fm = __half22float2(
+                    __floats2half2_rn(v[8 * j + 2 * q], v[8 * j + 2 * q + 1]));
                 const float2 fr = __half22float2(rh[q]);
-                ow[q] = pack_half2(fr.x + fm.x, fr.y + fm.y);
+                hw[4 * j + q] = pack_half2(fr.x + fm.x, fr.y + fm.y);
               }
-            } else {
-#pragma unroll
-              for (int q = 0; q < 4; ++q)
-                ow[q] = pack_half2(v[8 * g + 2 * q], v[8 * g + 2 * q + 1]);
             }
-            reinterpret_cast<uint4*>(orow + n0)[g] = o;
+          } else {
+#pragma unroll
+            for (int q = 0; q < 16; ++q) hw[q] = pack_half2(v[2 * q], v[2 * q + 1]);
           }
+          // 4 x 16 B into the 128-byte row rl of the stage, swizzled
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int chunk = (h * 4 + j) ^ (rl & 7);
+            *reinterpret_cast<uint4*>(stage + rl * 128 + chunk * 16) =
+                make_uint4(hw[4 * j], hw[4 * j + 1], hw[4 * j + 2], hw[4 * j + 3]);
+          }
+        }
+        fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_3d(&tmC, stage, nb * BN + g * 64, mb * BM + quarter * 32, (int)b);
+          bulk_commit_group();
         }
       }
       tc_fence_before();
@@ -270,6 +302,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
   }
 
 done:
@@ -365,6 +399,11 @@ int launch_tc(const GemmDesc& g, int* err, cudaStream_t s) {
   if (!make_tmap_3d_f16(&tb, g.B, (uint64_t)g.N, (uint64_t)g.K,
                         (uint64_t)(g.b_shared ? 1 : g.batch), 64, BK))
     return -1;
+  // out: dims (N, M, batch); box (64, 32, 1) -- one epilogue warp's slab.
+  CUtensorMap tcm;
+  if (!make_tmap_3d_f16(&tcm, g.out, (uint64_t)g.N, (uint64_t)g.M,
+                        (uint64_t)g.batch, 64, 32))
+    return -1;
   GemmParams p;
   p.M = g.M;
   p.K = g.K;
@@ -383,7 +422,7 @@ int launch_tc(const GemmDesc& g, int* err, cudaStream_t s) {
   const int64_t grid64 =
       p.total_tiles < sm_count() ? p.total_tiles : (int64_t)sm_count();
   gemm_f16_tc<BN><<<(int)grid64, kGemmThreads, Cfg::SMEM_BYTES, s>>>(ta, tb,
-                                                                      p);
+                                                                      tcm, p);
   if (cudaPeekAtLastError() != cudaSuccess) {
     cudaGetLastError();
     return HEXLIB_B200_ERR_CUDA;

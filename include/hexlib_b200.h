@@ -171,6 +171,14 @@ HEXLIB_B200_API int hexlib_b200_check_batch(const uint8_t *batch, uint32_t len,
                             uint32_t n_images, uint8_t *rsp, uint32_t rsp_cap,
                             uint32_t *rsp_len);
 
+/* Failure-path diagnostic: launch, on the session stream, a kernel whose
+ * bounded mbarrier wait is never satisfied; after `limit_us` (1..1e6) it
+ * records a timeout and returns. Answers HEXLIB_B200_ERR_TIMEOUT and leaves
+ * the session usable -- the same path a lost arrival in any pipelined kernel
+ * of this library takes. */
+HEXLIB_B200_API int hexlib_b200_diag_wait_timeout(hexlib_b200_ctx *ctx,
+                                                  uint32_t limit_us);
+
 /* The status as text (hexlib_dsp.h:71-91). */
 HEXLIB_B200_API const char *hexlib_b200_status_name(int status);
 
