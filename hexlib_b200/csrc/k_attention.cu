@@ -12,8 +12,9 @@
 //              K=64) into TMEM, and after the softmax has written P_t to shared
 //              memory, O_t = P_t V (M=128, N=64, K=128) into TMEM;
 //   warps 2-5  softmax of tile a, warps 6-9 softmax of tile b: one query row
-//              per thread, read from TMEM twice (row max, then exp2/sum/P),
-//              online rescaling of the running output held in registers.
+//              per thread, the block's scores read from TMEM in one pass,
+//              P written to shared memory; the output accumulates in TMEM and
+//              is rescaled there only when the running max grows by > 2^8.
 // While one tile's softmax runs, the tensor core works on the other tile's
 // products, so the exp units and the tensor core overlap.
 //
@@ -143,7 +144,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       constexpr uint32_t idesc_s = idesc_f16_f32(AT_BM, AT_BN, false, false);
       constexpr uint32_t idesc_o = idesc_f16_f32(AT_BM, AT_D, false, true);
       if (!mbar_wait(q_full, 0, abort_flag, p.err)) goto done;
-      // S_t(j) = Q_t K_j^T
+      // S_t(j) = Q_t K_j^T, once the softmax has read S_t(j-1) out of TMEM
       auto issue_s = [&](int t, int j) -> bool {
         const int st = j % AT_STAGES;
         if (!mbar_wait(&kv_full[st], (uint32_t)(j / AT_STAGES) & 1u, abort_flag, p.err))
@@ -160,7 +161,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         umma_commit(&s_full[t]);
         return true;
       };
-      // O_t(j) = P_t(j) V_j
+      // O_t += P_t(j) V_j (overwrite at j = 0); O_t stays in TMEM throughout
       auto issue_pv = [&](int t, int j) -> bool {
         const int st = j % AT_STAGES;
         if (!mbar_wait(&p_full[t], (uint32_t)j & 1u, abort_flag, p.err)) return false;
@@ -171,21 +172,29 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         for (int kk = 0; kk < AT_BN / 16; ++kk)
           umma_f16(tmem + 256u + (uint32_t)(t * AT_D),
                    sdesc_sw128(pa + (kk >> 2) * (AT_BM * 128) + (kk & 3) * 32, 16, 1024),
-                   sdesc_sw128(vb + kk * 2048, 8192, 1024), idesc_o, kk ? 1u : 0u);
+                   sdesc_sw128(vb + kk * 2048, 8192, 1024), idesc_o,
+                   (j > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&o_full[t]);
         return true;
       };
       if (!issue_s(0, 0) || !issue_s(1, 0)) goto done;
       for (int j = 0; j < nkv; ++j) {
-        if (!issue_pv(0, j)) goto done;
+        // S(j+1) goes in ahead of P(j)V(j), so a tile's next scores are ready
+        // by the time its softmax finishes the current block.
         if (j + 1 < nkv && !issue_s(0, j + 1)) goto done;
+        if (!issue_pv(0, j)) goto done;
+        if (j + 1 < nkv && !issue_s(1, j + 1)) goto done;
         if (!issue_pv(1, j)) goto done;
         umma_commit(&kv_empty[j % AT_STAGES]);   // K_j and V_j fully consumed
-        if (j + 1 < nkv && !issue_s(1, j + 1)) goto done;
       }
     }
   } else {
-    // softmax warpgroups: t = 0 (warps 2-5) or 1 (warps 6-9)
+    // Softmax warpgroups: t = 0 (warps 2-5) or 1 (warps 6-9), one query row
+    // per thread. The running output O_t accumulates in TMEM; its scale, the
+    // running max m_run, changes only when a block's max exceeds it by more
+    // than 2^8 ("lazy" rescaling: between rescales p = 2^(s*c - m_run) stays
+    // below 256, exactly representable in range by fp16 P), so most blocks
+    // never touch O at all.
     const int t = (warp - 2) >> 2;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;               // row within the tile
@@ -194,122 +203,114 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     const uint32_t o_col = tmem + lane_off + 256u + (uint32_t)(t * AT_D);
     uint8_t* prow = sP + t * AT_P + r * 128;
     const float c = p.c_log2;
-    float m_run = -INFINITY, l_run = 0.f, alpha_prev = 1.f;
-    float o[AT_D];
-#pragma unroll
-    for (int i = 0; i < AT_D; ++i) o[i] = 0.f;
+    constexpr float kRescale = 8.0f;
+    float m_run = -INFINITY, l_run = 0.f;
 
     for (int j = 0; j < nkv; ++j) {
       const bool ok = mbar_wait(&s_full[t], (uint32_t)j & 1u, abort_flag, p.err);
       if (!__all_sync(0xffffffffu, ok)) goto done;
       tc_fence_after();
-      const int key0 = j * AT_BN;
-      const int valid = p.T - key0;          // keys of this block that exist
-      // pass 1: row max of the raw scores, two 32-column chunks per TMEM
-      // round trip and eight independent partial maxima
+      uint32_t sv[AT_BN];
+#pragma unroll
+      for (int cc = 0; cc < AT_BN / 32; ++cc)
+        tmem_ld_32x32b_x32(s_col + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[cc * 32]));
+      tmem_ld_wait();
+      // S is in registers: hand its TMEM back for S(j+1)
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[t]);
+
+      const int valid = p.T - j * AT_BN;             // keys of this block that exist
+      if (valid < AT_BN) {
+#pragma unroll
+        for (int i = 0; i < AT_BN; ++i)
+          if (i >= valid) sv[i] = __float_as_uint(-INFINITY);
+      }
       float pm[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) pm[i] = -INFINITY;
+      for (int i = 0; i < 8; ++i) pm[i] = __uint_as_float(sv[i]);
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t ra[32], rb[32];
-        tmem_ld_32x32b_x32(s_col + half * 64, ra);
-        tmem_ld_32x32b_x32(s_col + half * 64 + 32, rb);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int ka = half * 64 + i, kb = half * 64 + 32 + i;
-          pm[i & 7] = fmaxf(pm[i & 7], ka < valid ? __uint_as_float(ra[i]) : -INFINITY);
-          pm[i & 7] = fmaxf(pm[i & 7], kb < valid ? __uint_as_float(rb[i]) : -INFINITY);
-        }
-      }
-      const float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
-                             fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
+      for (int i = 8; i < AT_BN; ++i) pm[i & 7] = fmaxf(pm[i & 7], __uint_as_float(sv[i]));
       // the scale is positive, so max(s)*c is the max of s*c
-      const float m_new = fmaxf(m_run, mx * c);
-      const float alpha = ex2_approx(m_run - m_new);
-      // fold the previous block's P V into the running output
+      const float mx = c * fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
+                                 fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
+      const bool rescale = mx > m_run + kRescale;
+      const float m_use = rescale ? mx : m_run;
+      const float alpha = rescale ? ex2_approx(m_run - mx) : 1.0f;
+      // p = 2^(s*c - m), eight partial row sums, packed to fp16
+      float ps[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ps[i] = 0.f;
+      uint32_t h2[AT_BN / 2];
+#pragma unroll
+      for (int i = 0; i < AT_BN / 2; ++i) {
+        const float p0 = ex2_approx(fmaf(__uint_as_float(sv[2 * i]), c, -m_use));
+        const float p1 = ex2_approx(fmaf(__uint_as_float(sv[2 * i + 1]), c, -m_use));
+        ps[i & 7] += p0 + p1;
+        h2[i] = pack_half2(p0, p1);
+      }
+      const float rs = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+      // P V of the previous block must be done: it reads the P buffer this
+      // block overwrites, and a rescale must see its contribution in O.
       if (j > 0) {
         const bool ok2 = mbar_wait(&o_full[t], (uint32_t)(j - 1) & 1u, abort_flag, p.err);
         if (!__all_sync(0xffffffffu, ok2)) goto done;
         tc_fence_after();
-        uint32_t ra[32], rb[32];
-        tmem_ld_32x32b_x32(o_col, ra);
-        tmem_ld_32x32b_x32(o_col + 32, rb);
-        tmem_ld_wait();
+        if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          o[i] = fmaf(o[i], alpha_prev, __uint_as_float(ra[i]));
-          o[32 + i] = fmaf(o[32 + i], alpha_prev, __uint_as_float(rb[i]));
+          for (int h = 0; h < AT_D / 32; ++h) {
+            uint32_t rg[32];
+            tmem_ld_32x32b_x32(o_col + h * 32, rg);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              rg[i] = __float_as_uint(__uint_as_float(rg[i]) * alpha);
+            tmem_st_32x32b_x32(o_col + h * 32, rg);
+          }
+          tmem_st_wait();
         }
       }
-      // pass 2: p = 2^(s*c - m), eight partial row sums, P to shared memory
-      float ps[8];
+      // P to shared memory: keys [64a, 64a + 64) form one 128-byte atom row
 #pragma unroll
-      for (int i = 0; i < 8; ++i) ps[i] = 0.f;
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t ra[32], rb[32];
-        tmem_ld_32x32b_x32(s_col + half * 64, ra);
-        tmem_ld_32x32b_x32(s_col + half * 64 + 32, rb);
-        tmem_ld_wait();
-        uint32_t h2[32];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int k0 = half * 64 + 2 * i;
-          const float p0 = k0 < valid ? ex2_approx(fmaf(__uint_as_float(ra[2 * i]), c, -m_new)) : 0.f;
-          const float p1 = k0 + 1 < valid ? ex2_approx(fmaf(__uint_as_float(ra[2 * i + 1]), c, -m_new)) : 0.f;
-          const float p2 = k0 + 32 < valid ? ex2_approx(fmaf(__uint_as_float(rb[2 * i]), c, -m_new)) : 0.f;
-          const float p3 = k0 + 33 < valid ? ex2_approx(fmaf(__uint_as_float(rb[2 * i + 1]), c, -m_new)) : 0.f;
-          ps[(2 * i) & 7] += p0 + p2;
-          ps[(2 * i + 1) & 7] += p1 + p3;
-          h2[i] = pack_half2(p0, p1);
-          h2[16 + i] = pack_half2(p2, p3);
-        }
-        // keys [half*64, half*64 + 64) are exactly one 128-byte atom row
-        uint8_t* atom = prow + half * (AT_BM * 128);
+      for (int a = 0; a < 2; ++a) {
+        uint8_t* atom = prow + a * (AT_BM * 128);
 #pragma unroll
         for (int g = 0; g < 8; ++g) {
           const int chunk = g ^ (r & 7);
+          const int q = a * 32 + 4 * g;
           *reinterpret_cast<uint4*>(atom + chunk * 16) =
-              make_uint4(h2[4 * g], h2[4 * g + 1], h2[4 * g + 2], h2[4 * g + 3]);
+              make_uint4(h2[q], h2[q + 1], h2[q + 2], h2[q + 3]);
         }
       }
-      const float rs = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
       tc_fence_before();
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&s_free[t]);
-        mbar_arrive(&p_full[t]);
-      }
+      if (lane == 0) mbar_arrive(&p_full[t]);
       l_run = l_run * alpha + rs;
-      m_run = m_new;
-      alpha_prev = alpha;
+      m_run = m_use;
     }
     {
       const bool ok = mbar_wait(&o_full[t], (uint32_t)(nkv - 1) & 1u, abort_flag, p.err);
       if (!__all_sync(0xffffffffu, ok)) goto done;
       tc_fence_after();
+      const int row = q0 + t * AT_BM + r;
+      const float inv = 1.0f / l_run;
+      uint4* dst = reinterpret_cast<uint4*>(p.out + (bn * p.T + row) * (int64_t)AT_D);
 #pragma unroll
       for (int h = 0; h < AT_D / 32; ++h) {
         uint32_t rg[32];
         tmem_ld_32x32b_x32(o_col + h * 32, rg);
         tmem_ld_wait();
+        if (row < p.T) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          o[h * 32 + i] = fmaf(o[h * 32 + i], alpha_prev, __uint_as_float(rg[i]));
-      }
-      const int row = q0 + t * AT_BM + r;
-      if (row < p.T) {
-        const float inv = 1.0f / l_run;
-        uint4* dst = reinterpret_cast<uint4*>(p.out + (bn * p.T + row) * (int64_t)AT_D);
-#pragma unroll
-        for (int g = 0; g < AT_D / 8; ++g)
-          dst[g] = make_uint4(pack_half2(o[8 * g] * inv, o[8 * g + 1] * inv),
-                              pack_half2(o[8 * g + 2] * inv, o[8 * g + 3] * inv),
-                              pack_half2(o[8 * g + 4] * inv, o[8 * g + 5] * inv),
-                              pack_half2(o[8 * g + 6] * inv, o[8 * g + 7] * inv));
+          for (int g = 0; g < 4; ++g) {
+            const float* o = reinterpret_cast<const float*>(&rg[8 * g]);
+            dst[h * 4 + g] = make_uint4(pack_half2(o[0] * inv, o[1] * inv),
+                                        pack_half2(o[2] * inv, o[3] * inv),
+                                        pack_half2(o[4] * inv, o[5] * inv),
+                                        pack_half2(o[6] * inv, o[7] * inv));
+          }
+        }
       }
     }
   }
