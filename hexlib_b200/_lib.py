@@ -67,6 +67,9 @@ _PROTOS: dict[str, list] = {
                                                   c_vp],
     "hexlib_b200_attention_fp16": [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int,
                                    c_f, c_vp],
+    "hexlib_b200_matmul_epilogue_rope_fp16": [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int,
+                                              c_int, c_int, c_int, c_int, c_int, c_vp],
+    "hexlib_b200_attention_qkv_fp16": [c_vp, c_vp, c_int, c_int, c_int, c_int, c_f, c_vp],
 }
 
 

@@ -332,6 +332,45 @@ int check_op(const OpRec& op) {
       if (op.params[0] < 0 || op.params[0] > 2) return HEXLIB_B200_ERR_INVAL_PARAMS;
       return HEXLIB_B200_OK;
     }
+    case HEXLIB_B200_KIND_MATMUL_EPILOGUE_ROPE: {
+      HB_TRY(need(op, 6));
+      HB_TRY(dt(op, 0, DT_FP16));
+      HB_TRY(dt(op, 1, DT_FP16));
+      HB_TRY(dt(op, 2, DT_FP32));
+      HB_TRY(dt(op, 3, DT_FP32));
+      HB_TRY(dt(op, 4, DT_FP32));
+      HB_TRY(dt(op, 5, DT_FP16));
+      HB_TRY(batching(op, 5));
+      const uint32_t* a = op.a[0].ne;   // M, K
+      const uint32_t* w = op.a[1].ne;   // K, N
+      const uint32_t* c = op.a[3].ne;   // T, 64
+      if (a[2] != 1 || a[3] != 1 || w[2] != 1 || w[3] != 1 || w[0] != a[1] || a[1] == 0 ||
+          w[1] == 0 || numel(op.a[2].ne) != w[1] || op.a[1].per_image ||
+          op.a[2].per_image || op.a[3].per_image || op.a[4].per_image ||
+          memcmp(op.a[3].ne, op.a[4].ne, sizeof(uint32_t) * 4) != 0 || c[1] != 64 ||
+          c[2] != 1 || c[3] != 1 || c[0] == 0 || a[0] % c[0] != 0 ||
+          numel(op.a[5].ne) != (uint64_t)a[0] * w[1])
+        return HEXLIB_B200_ERR_INVAL_PARAMS;
+      if (op.params[0] < 0 || op.params[0] > 2 || op.params[1] <= 0 || op.params[1] % 64 ||
+          (uint32_t)op.params[1] > w[1] || w[1] % 64)
+        return HEXLIB_B200_ERR_INVAL_PARAMS;
+      return HEXLIB_B200_OK;
+    }
+    case HEXLIB_B200_KIND_ATTENTION_QKV: {
+      HB_TRY(need(op, 2));
+      HB_TRY(dt(op, 0, DT_FP16));
+      HB_TRY(dt(op, 1, DT_FP16));
+      HB_TRY(batching(op, 1));
+      const uint32_t* x = op.a[0].ne;   // T, 3, H, D
+      const uint32_t* y = op.a[1].ne;   // T, H, D
+      if (x[1] != 3 || x[3] != 64 || x[0] == 0 || x[2] == 0 || y[0] != x[0] ||
+          y[1] != x[2] || y[2] != x[3] || y[3] != 1)
+        return HEXLIB_B200_ERR_INVAL_PARAMS;
+      float sc;
+      memcpy(&sc, &op.params[0], 4);
+      if (!(sc > 0.f)) return HEXLIB_B200_ERR_INVAL_PARAMS;
+      return HEXLIB_B200_OK;
+    }
     case HEXLIB_B200_KIND_ATTENTION: {
       HB_TRY(need(op, 4));
       for (int i = 0; i < 4; ++i) HB_TRY(dt(op, i, DT_FP16));
@@ -443,6 +482,27 @@ int run_op(const OpRec& op, uint32_t n_images, int* err, cudaStream_t s) {
       g.act = op.params[0];
       return hb::launch_gemm(g, err, s);
     }
+    case HEXLIB_B200_KIND_MATMUL_EPILOGUE_ROPE: {
+      hb::GemmDesc g{};
+      g.A = a[0].ptr;
+      g.B = a[1].ptr;
+      g.bias = (const float*)a[2].ptr;
+      g.out = a[5].ptr;
+      g.batch = 1;
+      g.M = (int64_t)a[0].ne[0] * B;
+      g.K = (int)a[0].ne[1];
+      g.N = (int)a[1].ne[1];
+      g.b_shared = true;
+      g.act = op.params[0];
+      g.rope_cos = (const float*)a[3].ptr;
+      g.rope_sin = (const float*)a[4].ptr;
+      g.rope_T = (int)a[3].ne[0];
+      g.rope_cols = op.params[1];
+      return hb::launch_gemm(g, err, s);
+    }
+    case HEXLIB_B200_KIND_ATTENTION_QKV:
+      return hb::launch_attention_qkv(a[0].ptr, a[1].ptr, B, (int)a[0].ne[0], (int)a[0].ne[2],
+                                      (int)a[0].ne[3], param_f(op, 0), err, s);
     case HEXLIB_B200_KIND_ATTENTION:
       return hb::launch_attention(a[0].ptr, a[1].ptr, a[2].ptr, a[3].ptr,
                                   (int64_t)a[0].ne[0] * B, (int)a[0].ne[1],

@@ -212,6 +212,39 @@ int hexlib_b200_matmul_epilogue_residual_fp16(const void* a, const void* w,
   return hb::launch_gemm(g, hb::default_error_word(), as_stream(stream));
 }
 
+int hexlib_b200_matmul_epilogue_rope_fp16(const void* a, const void* w, const float* bias,
+                                          const float* costab, const float* sintab, void* out,
+                                          int M, int K, int N, int act, int rope_cols, int T,
+                                          void* stream) {
+  HB_ENTRY_INIT();
+  if (M < 0 || K <= 0 || N <= 0 || act < 0 || act > 2 || !bias || !costab || !sintab ||
+      rope_cols <= 0 || T <= 0 || (M % T) != 0)
+    return HEXLIB_B200_ERR_INVAL_PARAMS;
+  hb::GemmDesc g{};
+  g.A = a;
+  g.B = w;
+  g.bias = bias;
+  g.out = out;
+  g.batch = 1;
+  g.M = M;
+  g.K = K;
+  g.N = N;
+  g.b_shared = true;
+  g.act = act;
+  g.rope_cos = costab;
+  g.rope_sin = sintab;
+  g.rope_T = T;
+  g.rope_cols = rope_cols;
+  return hb::launch_gemm(g, hb::default_error_word(), as_stream(stream));
+}
+
+int hexlib_b200_attention_qkv_fp16(const void* qkv, void* ctx, int B, int T, int H, int D,
+                                   float scale, void* stream) {
+  HB_ENTRY_INIT();
+  return hb::launch_attention_qkv(qkv, ctx, B, T, H, D, scale, hb::default_error_word(),
+                                  as_stream(stream));
+}
+
 int hexlib_b200_attention_fp16(const void* q, const void* k, const void* v,
                                void* ctx, int Bn, int T, int D, float scale,
                                void* stream) {

@@ -64,6 +64,13 @@ struct GemmDesc {
   int K, N;
   bool b_shared;       // B has one copy used by every batch entry
   int act;             // 0 none, 1 gelu_tanh, 2 gelu_erf
+  // RoPE epilogue: when rope_cols > 0, columns [0, rope_cols) are 64-wide
+  // heads rotated with row r's token r % rope_T of the [rope_T, 64] tables,
+  // after the fp16 rounding of act(A@W + bias) (the rope_2d op on q/k).
+  const float* rope_cos = nullptr;
+  const float* rope_sin = nullptr;
+  int rope_T = 0;
+  int rope_cols = 0;
 };
 int launch_gemm(const GemmDesc& g, int* err, cudaStream_t s);
 
@@ -71,6 +78,11 @@ int launch_gemm(const GemmDesc& g, int* err, cudaStream_t s);
 int launch_attention(const void* q, const void* k, const void* v, void* ctx,
                      int64_t Bn, int T, int D, float scale, int* err,
                      cudaStream_t s);
+
+// Fused attention over a packed projection: qkv is [B, T, 3, H, D] (q, k, v
+// sections of each token row), ctx is [B, T, H, D]. D must be 64.
+int launch_attention_qkv(const void* qkv, void* ctx, int64_t B, int T, int H, int D,
+                         float scale, int* err, cudaStream_t s);
 
 // Diagnostic: a kernel whose bounded wait never completes; it records a
 // timeout in `err` after `limit_us` and returns.

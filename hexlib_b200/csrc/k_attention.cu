@@ -49,10 +49,12 @@ constexpr uint32_t AT_TMEM_COLS = 512;           // S_a, S_b: 128 each; O_a, O_b
 
 struct AttnParams {
   int T;
-  int64_t Bn;
+  int64_t Bn;         // heads in total (images x H)
+  int H;              // heads per image: head h of image b is work item b*H + h
   int q_pairs;        // ceil(T / 256)
+  int xq, xk, xv;     // x (column) origin of q, k, v in their tensor maps
   float c_log2;       // scale * log2(e)
-  __half* out;
+  __half* out;        // row (b, t) of head h at ((b*T + t)*H + h)*64
   int* err;
 };
 
@@ -92,7 +94,9 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int64_t bn = blockIdx.x / p.q_pairs;
+  const int64_t bh = blockIdx.x / p.q_pairs;
+  const int bimg = (int)(bh / p.H);
+  const int head = (int)(bh % p.H);
   const int q0 = (int)(blockIdx.x % p.q_pairs) * (2 * AT_BM);
   const int nkv = (p.T + AT_BN - 1) / AT_BN;
 
@@ -128,15 +132,15 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   if (warp == 0) {
     if (lane == 0) {
       mbar_arrive_expect_tx(q_full, 2 * AT_TILE);
-      tma_load_3d(&tmQ, q_full, sQ, 0, q0, (int)bn);
-      tma_load_3d(&tmQ, q_full, sQ + AT_TILE, 0, q0 + AT_BM, (int)bn);
+      tma_load_3d(&tmQ, q_full, sQ, p.xq + head * AT_D, q0, bimg);
+      tma_load_3d(&tmQ, q_full, sQ + AT_TILE, p.xq + head * AT_D, q0 + AT_BM, bimg);
       for (int j = 0; j < nkv; ++j) {
         const int st = j % AT_STAGES;
         const uint32_t ph = (uint32_t)(j / AT_STAGES) & 1u;
         if (!mbar_wait(&kv_empty[st], ph ^ 1u, abort_flag, p.err)) goto done;
         mbar_arrive_expect_tx(&kv_full[st], 2 * AT_TILE);
-        tma_load_3d(&tmK, &kv_full[st], sK + st * AT_TILE, 0, j * AT_BN, (int)bn);
-        tma_load_3d(&tmV, &kv_full[st], sV + st * AT_TILE, 0, j * AT_BN, (int)bn);
+        tma_load_3d(&tmK, &kv_full[st], sK + st * AT_TILE, p.xk + head * AT_D, j * AT_BN, bimg);
+        tma_load_3d(&tmV, &kv_full[st], sV + st * AT_TILE, p.xv + head * AT_D, j * AT_BN, bimg);
       }
     }
   } else if (warp == 1) {
@@ -295,7 +299,8 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       tc_fence_after();
       const int row = q0 + t * AT_BM + r;
       const float inv = 1.0f / l_run;
-      uint4* dst = reinterpret_cast<uint4*>(p.out + (bn * p.T + row) * (int64_t)AT_D);
+      uint4* dst = reinterpret_cast<uint4*>(
+          p.out + (((int64_t)bimg * p.T + row) * p.H + head) * (int64_t)AT_D);
 #pragma unroll
       for (int h = 0; h < AT_D / 32; ++h) {
         uint32_t rg[32];
@@ -398,6 +403,8 @@ int launch_attention(const void* q, const void* k, const void* v, void* ctx, int
       AttnParams p;
       p.T = T;
       p.Bn = Bn;
+      p.H = 1;
+      p.xq = p.xk = p.xv = 0;
       p.q_pairs = (T + 2 * AT_BM - 1) / (2 * AT_BM);
       p.c_log2 = scale * 1.4426950408889634f;
       p.out = reinterpret_cast<__half*>(ctx);
@@ -418,6 +425,40 @@ int launch_attention(const void* q, const void* k, const void* v, void* ctx, int
   attention_simt<256><<<(unsigned)blocks, 128, 0, s>>>(
       reinterpret_cast<const __half*>(q), reinterpret_cast<const __half*>(k),
       reinterpret_cast<const __half*>(v), reinterpret_cast<__half*>(ctx), Bn, T, D, scale);
+  if (cudaPeekAtLastError() != cudaSuccess) {
+    cudaGetLastError();
+    return HEXLIB_B200_ERR_CUDA;
+  }
+  return HEXLIB_B200_OK;
+}
+
+int launch_attention_qkv(const void* qkv, void* ctx, int64_t B, int T, int H, int D,
+                         float scale, int* err, cudaStream_t s) {
+  if (B < 0 || T <= 0 || H <= 0 || D <= 0) return HEXLIB_B200_ERR_INVAL_PARAMS;
+  if (B == 0) return HEXLIB_B200_OK;
+  if (!qkv || !ctx) return HEXLIB_B200_ERR_INVAL_PARAMS;
+  // The packed layout [B, T, 3, H, D] is served by the tensor-core kernel
+  // only: one 3-D map over rows of 3*H*D columns, q/k/v at column offsets.
+  if (D != AT_D || scale <= 0.f || !aligned16(qkv) || !aligned16(ctx) || !tma_available() ||
+      B * H >= ((int64_t)1 << 30) || B >= ((int64_t)1 << 31))
+    return HEXLIB_B200_ERR_INVAL_PARAMS;
+  const uint64_t W = (uint64_t)3 * H * D;
+  CUtensorMap m;
+  if (!make_tmap_3d_f16(&m, qkv, W, (uint64_t)T, (uint64_t)B, 64, AT_BM))
+    return HEXLIB_B200_ERR_INVAL_PARAMS;
+  AttnParams p;
+  p.T = T;
+  p.Bn = B * H;
+  p.H = H;
+  p.xq = 0;
+  p.xk = H * D;
+  p.xv = 2 * H * D;
+  p.q_pairs = (T + 2 * AT_BM - 1) / (2 * AT_BM);
+  p.c_log2 = scale * 1.4426950408889634f;
+  p.out = reinterpret_cast<__half*>(ctx);
+  p.err = err;
+  const int64_t grid = p.Bn * p.q_pairs;
+  attention_tc<<<(unsigned)grid, AT_THREADS, AT_SMEM, s>>>(m, m, m, p);
   if (cudaPeekAtLastError() != cudaSuccess) {
     cudaGetLastError();
     return HEXLIB_B200_ERR_CUDA;

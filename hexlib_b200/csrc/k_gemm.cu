@@ -69,9 +69,49 @@ struct GemmParams {
   const __half* resid;
   __half* out;
   int* err;
+  // RoPE epilogue (ROPE kernels only): columns [0, rope_cols) are heads of
+  // 64; row r is token r % rope_T of the [rope_T, 64] cos/sin tables.
+  const float* rope_cos;
+  const float* rope_sin;
+  int rope_T;
+  int rope_cols;
 };
 
-template <int BN>
+// Split-half rotation of one 64-column head (kernels/rope_2d_fp16/kernel_api.h:
+// 17-26) applied to fp16-rounded inputs with separately rounded products, as
+// the rope_2d op computes it on the stored q/k.
+__device__ __forceinline__ void rope_head64(uint32_t (&lo)[16], uint32_t (&hi)[16],
+                                            const float* __restrict__ ct,
+                                            const float* __restrict__ st) {
+#pragma unroll
+  for (int i = 0; i < 16; i += 4) {
+    const float4 c0 = __ldg(reinterpret_cast<const float4*>(ct + 2 * i));
+    const float4 c1 = __ldg(reinterpret_cast<const float4*>(ct + 2 * i + 4));
+    const float4 c2 = __ldg(reinterpret_cast<const float4*>(ct + 32 + 2 * i));
+    const float4 c3 = __ldg(reinterpret_cast<const float4*>(ct + 32 + 2 * i + 4));
+    const float4 s0 = __ldg(reinterpret_cast<const float4*>(st + 2 * i));
+    const float4 s1 = __ldg(reinterpret_cast<const float4*>(st + 2 * i + 4));
+    const float4 s2 = __ldg(reinterpret_cast<const float4*>(st + 32 + 2 * i));
+    const float4 s3 = __ldg(reinterpret_cast<const float4*>(st + 32 + 2 * i + 4));
+    const float cl[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    const float ch[8] = {c2.x, c2.y, c2.z, c2.w, c3.x, c3.y, c3.z, c3.w};
+    const float sl[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    const float sh[8] = {s2.x, s2.y, s2.z, s2.w, s3.x, s3.y, s3.z, s3.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&lo[i + q]));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&hi[i + q]));
+      const float y0 = __fadd_rn(__fmul_rn(a.x, cl[2 * q]), __fmul_rn(-b.x, sl[2 * q]));
+      const float y1 = __fadd_rn(__fmul_rn(a.y, cl[2 * q + 1]), __fmul_rn(-b.y, sl[2 * q + 1]));
+      const float z0 = __fadd_rn(__fmul_rn(b.x, ch[2 * q]), __fmul_rn(a.x, sh[2 * q]));
+      const float z1 = __fadd_rn(__fmul_rn(b.y, ch[2 * q + 1]), __fmul_rn(a.y, sh[2 * q + 1]));
+      lo[i + q] = pack_half2(y0, y1);
+      hi[i + q] = pack_half2(z0, z1);
+    }
+  }
+}
+
+template <int BN, bool ROPE>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_f16_tc(const __grid_constant__ CUtensorMap tmA,
                 const __grid_constant__ CUtensorMap tmB,
@@ -224,6 +264,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // the previous group's store must have finished reading the stage
         if (lane == 0) bulk_wait_read_all();
         __syncwarp();
+        uint32_t packed[2][16];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           const int c32 = g * 64 + h * 32;          // column within the tile
@@ -281,14 +322,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
             for (int q = 0; q < 16; ++q) hw[q] = pack_half2(v[2 * q], v[2 * q + 1]);
           }
-          // 4 x 16 B into the 128-byte row rl of the stage, swizzled
+#pragma unroll
+          for (int q = 0; q < 16; ++q) packed[h][q] = hw[q];
+        }
+        if (ROPE) {
+          const int n64 = nb * BN + g * 64;
+          if (n64 < p.rope_cols && row_ok) {
+            const int tok = (int)(row % p.rope_T);
+            rope_head64(packed[0], packed[1], p.rope_cos + (int64_t)tok * 64,
+                        p.rope_sin + (int64_t)tok * 64);
+          }
+        }
+        // 8 x 16 B into the 128-byte row rl of the stage, swizzled
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const int chunk = (h * 4 + j) ^ (rl & 7);
             *reinterpret_cast<uint4*>(stage + rl * 128 + chunk * 16) =
-                make_uint4(hw[4 * j], hw[4 * j + 1], hw[4 * j + 2], hw[4 * j + 3]);
+                make_uint4(packed[h][4 * j], packed[h][4 * j + 1], packed[h][4 * j + 2],
+                           packed[h][4 * j + 3]);
           }
-        }
         fence_proxy_async_shared();
         __syncwarp();
         if (lane == 0) {
@@ -387,7 +441,7 @@ int sm_count() {
   return g_sm_count;
 }
 
-template <int BN>
+template <int BN, bool ROPE>
 int launch_tc(const GemmDesc& g, int* err, cudaStream_t s) {
   using Cfg = GemmCfg<BN>;
   CUtensorMap ta, tb;
@@ -419,10 +473,14 @@ int launch_tc(const GemmDesc& g, int* err, cudaStream_t s) {
   p.resid = reinterpret_cast<const __half*>(g.resid);
   p.out = reinterpret_cast<__half*>(g.out);
   p.err = err;
+  p.rope_cos = g.rope_cos;
+  p.rope_sin = g.rope_sin;
+  p.rope_T = g.rope_T > 0 ? g.rope_T : 1;
+  p.rope_cols = ROPE ? g.rope_cols : 0;
   const int64_t grid64 =
       p.total_tiles < sm_count() ? p.total_tiles : (int64_t)sm_count();
-  gemm_f16_tc<BN><<<(int)grid64, kGemmThreads, Cfg::SMEM_BYTES, s>>>(ta, tb,
-                                                                      tcm, p);
+  gemm_f16_tc<BN, ROPE><<<(int)grid64, kGemmThreads, Cfg::SMEM_BYTES, s>>>(ta, tb,
+                                                                            tcm, p);
   if (cudaPeekAtLastError() != cudaSuccess) {
     cudaGetLastError();
     return HEXLIB_B200_ERR_CUDA;
@@ -438,16 +496,28 @@ bool aligned16(const void* p) {
 
 int gemm_kernels_init() {
   cudaError_t e1 = cudaFuncSetAttribute(
-      gemm_f16_tc<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      gemm_f16_tc<64, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
       GemmCfg<64>::SMEM_BYTES);
   cudaError_t e2 = cudaFuncSetAttribute(
-      gemm_f16_tc<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      gemm_f16_tc<128, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
       GemmCfg<128>::SMEM_BYTES);
   cudaError_t e3 = cudaFuncSetAttribute(
-      gemm_f16_tc<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      gemm_f16_tc<256, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
       GemmCfg<256>::SMEM_BYTES);
+  cudaError_t e4 = cudaFuncSetAttribute(
+      gemm_f16_tc<256, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      GemmCfg<256>::SMEM_BYTES);
+  cudaError_t e5 = cudaFuncSetAttribute(
+      gemm_f16_tc<128, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      GemmCfg<128>::SMEM_BYTES);
+  cudaError_t e6 = cudaFuncSetAttribute(
+      gemm_f16_tc<64, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      GemmCfg<64>::SMEM_BYTES);
+  cudaFuncAttributes fa;
+  cudaError_t e7 = cudaFuncGetAttributes(&fa, gemm_f16_simt);
   sm_count();
-  if (e1 != cudaSuccess || e2 != cudaSuccess || e3 != cudaSuccess) {
+  if (e1 != cudaSuccess || e2 != cudaSuccess || e3 != cudaSuccess || e4 != cudaSuccess ||
+      e5 != cudaSuccess || e6 != cudaSuccess || e7 != cudaSuccess) {
     cudaGetLastError();
     return HEXLIB_B200_ERR_CUDA;
   }
@@ -459,6 +529,11 @@ int launch_gemm(const GemmDesc& g, int* err, cudaStream_t s) {
       g.act > 2 || !g.A || !g.B || !g.out)
     return HEXLIB_B200_ERR_INVAL_PARAMS;
   if (g.batch == 0 || g.M == 0) return HEXLIB_B200_OK;
+  const bool rope = g.rope_cols > 0;
+  if (rope && (g.rope_cols % 64 || g.rope_cols > g.N || g.N % 64 || g.rope_T <= 0 ||
+               !g.rope_cos || !g.rope_sin || !aligned16(g.rope_cos) ||
+               !aligned16(g.rope_sin)))
+    return HEXLIB_B200_ERR_INVAL_PARAMS;
   const bool tma_ok = (g.K % 8) == 0 && (g.N % 8) == 0 && aligned16(g.A) &&
                       aligned16(g.B) && aligned16(g.out) &&
                       (!g.bias || aligned16(g.bias)) &&
@@ -466,12 +541,13 @@ int launch_gemm(const GemmDesc& g, int* err, cudaStream_t s) {
   if (tma_ok) {
     int rc;
     if (g.N % 256 == 0)
-      rc = launch_tc<256>(g, err, s);
+      rc = rope ? launch_tc<256, true>(g, err, s) : launch_tc<256, false>(g, err, s);
     else if (g.N % 128 == 0)
-      rc = launch_tc<128>(g, err, s);
+      rc = rope ? launch_tc<128, true>(g, err, s) : launch_tc<128, false>(g, err, s);
     else
-      rc = launch_tc<64>(g, err, s);
+      rc = rope ? launch_tc<64, true>(g, err, s) : launch_tc<64, false>(g, err, s);
     if (rc != -1) return rc;
+    if (rope) return HEXLIB_B200_ERR_INVAL_PARAMS;  // no CUDA-core rope path
     // The tensor map was refused on the host: fall through to CUDA cores.
   }
   const int tiles_m = (int)((g.M + 63) / 64), tiles_n = (g.N + 63) / 64;

@@ -458,6 +458,114 @@ def fuse_residual(graph: Graph) -> Graph:
     return Graph(tensors, tuple(ops), graph.inputs, graph.outputs)
 
 
+def fuse_qkv(graph: Graph) -> tuple[Graph, dict[str, tuple]]:
+    """CUDA-only, after `fuse_attention`: per block, the q, k and v projections
+    (three matmul_epilogue over one input), their reshapes to [T, H, D], the
+    rope_2d of q and k, the three [T,H,D] -> [H,T,D] transposes into the
+    attention op and the transpose of its output back to [T, H, D] become
+
+        qkv   = matmul_epilogue_rope(a, [wq|wk|wv], [bq|bk|bv], cos, sin)  [T, 3, H, D]
+        ctx.t = attention_qkv(qkv)                                         [T, H, D]
+
+    The concatenated weight and bias are new consts, returned as
+    `{name: ("concat", (parts...), axis)}` for the batch builder to derive from
+    the feeds. Every removed intermediate must have exactly one consumer and
+    not be a graph output; anything else leaves the block as it was."""
+    cons = _consumers(graph)
+    protected = set(graph.outputs)
+    producer = {o.outputs[0]: o for o in graph.ops}
+    T = graph.tensors
+
+    def sole_user(name):
+        c = cons.get(name, [])
+        return c[0] if len(c) == 1 and name not in protected else None
+
+    def prod(name, kind):
+        o = producer.get(name)
+        return o if o is not None and o.kind == kind and sole_user(name) is not None else None
+
+    consumed: set[int] = set()
+    rewritten: dict[int, Op] = {}
+    new_tensors: dict[str, Tensor] = {}
+    dropped: set[str] = set()
+    derived: dict[str, tuple] = {}
+    for att in graph.ops:
+        if att.kind != "attention":
+            continue
+        chain = {}
+        ok = True
+        for which, name, roped in (("q", att.inputs[0], True), ("k", att.inputs[1], True),
+                                   ("v", att.inputs[2], False)):
+            tr = prod(name, "transpose")
+            if tr is None or tuple(tr.attrs.get("perm", ())) != (1, 0, 2):
+                ok = False
+                break
+            rp = prod(tr.inputs[0], "rope_2d") if roped else None
+            if roped and rp is None:
+                ok = False
+                break
+            rs = prod((rp.inputs[0] if roped else tr.inputs[0]), "reshape")
+            mm = prod(rs.inputs[0], "matmul_epilogue") if rs is not None else None
+            if mm is None or mm.attrs.get("act", "none") != "none":
+                ok = False
+                break
+            chain[which] = (tr, rp, rs, mm)
+        if not ok:
+            continue
+        ctx_t = sole_user(att.outputs[0])
+        if ctx_t is None or ctx_t.kind != "transpose" or tuple(ctx_t.attrs.get("perm", ())) != (1, 0, 2):
+            continue
+        mms = [chain[w][3] for w in "qkv"]
+        a = mms[0].inputs[0]
+        if any(m.inputs[0] != a for m in mms):
+            continue
+        rq, rk = chain["q"][1], chain["k"][1]
+        if rq.inputs[1:] != rk.inputs[1:]:
+            continue
+        cos, sin = rq.inputs[1], rq.inputs[2]
+        ws = [m.inputs[1] for m in mms]
+        bs = [m.inputs[2] for m in mms]
+        if not all(T[w].const and T[w].dtype == "fp16" and len(T[w].shape) == 2 for w in ws):
+            continue
+        if not all(T[b].const and T[b].dtype == "fp32" for b in bs):
+            continue
+        n_tok, heads, d = T[att.outputs[0]].shape[1], T[att.outputs[0]].shape[0], T[att.outputs[0]].shape[2]
+        K = T[ws[0]].shape[0]
+        if any(T[w].shape != (K, heads * d) for w in ws) or T[a].shape != (n_tok, K) or d != 64:
+            continue
+        wname = f"concat({ws[0]},{ws[1]},{ws[2]})"
+        bname = f"concat({bs[0]},{bs[1]},{bs[2]})"
+        qkv = f"{mms[0].outputs[0]}+qkv"
+        new_tensors[wname] = Tensor(wname, "fp16", (K, 3 * heads * d), True)
+        new_tensors[bname] = Tensor(bname, "fp32", (3 * heads * d,), True)
+        new_tensors[qkv] = Tensor(qkv, "fp16", (n_tok, 3, heads, d), False)
+        derived[wname] = ("concat", tuple(ws), 1)
+        derived[bname] = ("concat", tuple(bs), 0)
+        rewritten[mms[0].id] = Op(mms[0].id, "matmul_epilogue_rope", (a, wname, bname, cos, sin),
+                                  (qkv,), {"act": "none", "rope_cols": 2 * heads * d})
+        rewritten[ctx_t.id] = Op(ctx_t.id, "attention_qkv", (qkv,), ctx_t.outputs,
+                                 {"scale": float(att.attrs["scale"])})
+        for w in "qkv":
+            tr, rp, rs, mm = chain[w]
+            for o in (tr, rp, rs, mm):
+                if o is not None:
+                    consumed.add(o.id)
+                    dropped.add(o.outputs[0])
+        consumed.add(att.id)
+        dropped.add(att.outputs[0])
+        consumed.discard(mms[0].id)
+    if not rewritten:
+        return graph, {}
+    ops = tuple(rewritten.get(o.id, o) for o in graph.ops
+                if o.id not in consumed or o.id in rewritten)
+    tensors = {n: t for n, t in graph.tensors.items() if n not in dropped}
+    tensors.update(new_tensors)
+    used = {n for o in ops for n in o.inputs}
+    tensors = {n: t for n, t in tensors.items()
+               if not (t.const and n not in used)}
+    return Graph(tensors, ops, graph.inputs, graph.outputs), derived
+
+
 # ---- the executable plan -------------------------------------------------------------
 
 @dataclass(frozen=True)
@@ -469,9 +577,12 @@ class Step:
 class ExecPlan:
     """What the CUDA path executes: the post-fusion graph and its op order.
     Shaped like the reference's `Compiled(graph, plan)` (compiled.py:33-66)
-    where the batch builder reads it: `.graph` and `.plan.steps[i].op`."""
+    where the batch builder reads it: `.graph` and `.plan.steps[i].op`.
+    `derived` names consts a rewrite created, with the recipe that builds
+    each from the feeds (`("concat", parts, axis)`)."""
     graph: Graph
     plan: "ExecSteps"
+    derived: Mapping[str, tuple] = field(default_factory=dict)
 
 
 @dataclass(frozen=True)
@@ -480,37 +591,42 @@ class ExecSteps:
     target: str = "b200"
 
 
-def compile_for_cuda(graph: Graph, attention: bool = False,
-                     residual: bool = False) -> ExecPlan:
-    """Fuse (as the reference pipeline does), optionally apply the CUDA-only
-    rewrites, and order the ops for execution (the builder's order is
-    topological; every rewrite keeps it so)."""
-    problems = graph.problems()
-    if problems:
-        raise ValueError("graph is structurally invalid: " + "; ".join(problems[:5]))
-    g = fuse(graph)
-    if attention:
+def _apply_rewrites(g: Graph, attention: bool, residual: bool, qkv: bool):
+    derived: dict[str, tuple] = {}
+    if attention or qkv:
         g = fuse_attention(g)
+    if qkv:
+        g, derived = fuse_qkv(g)
     if residual:
         g = fuse_residual(g)
     problems = g.problems()
     if problems:
         raise ValueError("rewritten graph is invalid: " + "; ".join(problems[:5]))
-    return ExecPlan(g, ExecSteps(tuple(Step(o) for o in g.ops)))
+    return g, derived
 
 
-def rewrite_compiled(compiled, attention: bool = False, residual: bool = False) -> ExecPlan:
+def compile_for_cuda(graph: Graph, attention: bool = False, residual: bool = False,
+                     qkv: bool = False) -> ExecPlan:
+    """Fuse (as the reference pipeline does), optionally apply the CUDA-only
+    rewrites, and order the ops for execution (the builder's order is
+    topological; every rewrite keeps it so). `qkv` implies `attention`."""
+    problems = graph.problems()
+    if problems:
+        raise ValueError("graph is structurally invalid: " + "; ".join(problems[:5]))
+    g, derived = _apply_rewrites(fuse(graph), attention, residual, qkv)
+    return ExecPlan(g, ExecSteps(tuple(Step(o) for o in g.ops)), derived)
+
+
+def rewrite_compiled(compiled, attention: bool = False, residual: bool = False,
+                     qkv: bool = False) -> ExecPlan:
     """Apply the CUDA-only rewrites to any compiled pair -- the reference's
     own `Compiled` included -- keeping its plan order for the ops that stay."""
     graph = as_graph(compiled.graph)
     order = [s.op.id for s in compiled.plan.steps if getattr(s, "op", None) is not None]
     by_id = {o.id: o for o in graph.ops}
     g = Graph(graph.tensors, tuple(by_id[i] for i in order), graph.inputs, graph.outputs)
-    if attention:
-        g = fuse_attention(g)
-    if residual:
-        g = fuse_residual(g)
-    return ExecPlan(g, ExecSteps(tuple(Step(o) for o in g.ops)))
+    g, derived = _apply_rewrites(g, attention, residual, qkv)
+    return ExecPlan(g, ExecSteps(tuple(Step(o) for o in g.ops)), derived)
 
 
 def as_graph(g) -> Graph:

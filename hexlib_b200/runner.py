@@ -17,8 +17,9 @@ DIFFERENCES FROM THE DSP's TABLE, each deliberate:
     table to fp16 as the DSP spec does (runner.py:395-398).
   * reshape has a variant (a device copy): the batch builder still elides
     reshapes by aliasing, but a blob that carries one is served.
-  * three ids are appended: attention (13), rmsnorm (14),
-    matmul_epilogue_residual (15).
+  * ids are appended for kernels the DSP table does not have: attention (13),
+    rmsnorm (14), matmul_epilogue_residual (15), matmul_epilogue_rope (16)
+    and attention_qkv (17).
 """
 from __future__ import annotations
 
@@ -43,6 +44,8 @@ KIND_ID: dict[str, int] = {
     "attention": 13,
     "rmsnorm": 14,
     "matmul_epilogue_residual": 15,
+    "matmul_epilogue_rope": 16,
+    "attention_qkv": 17,
 }
 
 ACT_CODES = (("none", 0), ("gelu_tanh", 1), ("gelu_erf", 2))
@@ -141,6 +144,13 @@ SPECS: dict[str, CudaSpec] = {
         "matmul_epilogue_residual", (F16, F16, F32, F16), "fp16",
         params=(Param("act", "int", ACT_CODES),),
         entry="hexlib_b200_matmul_epilogue_residual_fp16"),
+    "matmul_epilogue_rope": CudaSpec(
+        "matmul_epilogue_rope", (F16, F16, F32, F32, F32), "fp16",
+        params=(Param("act", "int", ACT_CODES), Param("rope_cols")),
+        entry="hexlib_b200_matmul_epilogue_rope_fp16"),
+    "attention_qkv": CudaSpec("attention_qkv", (F16,), "fp16",
+                              params=(Param("scale", "float"),),
+                              entry="hexlib_b200_attention_qkv_fp16"),
 }
 
 

@@ -226,14 +226,25 @@ def build_cuda_plan(compiled, feeds: Mapping[str, Any] | None = None,
 
     # ---- stage consts --------------------------------------------------------------
     payload = None
+    derived = dict(getattr(compiled, "derived", {}) or {})
     if feeds is not None:
         payload = bytearray(const_bytes)
         for n, p in placements.items():
             if p.region != "const":
                 continue
-            if n not in feeds:
+            if n in derived:
+                how, parts, axis = derived[n]
+                if how != "concat":
+                    raise WholePlanError(f"const {n!r}: unknown derivation {how!r}")
+                missing = [q for q in parts if q not in feeds]
+                if missing:
+                    raise WholePlanError(f"const {n!r} is built from {missing}, not supplied")
+                value = np.concatenate([np.asarray(feeds[q]) for q in parts], axis=axis)
+            elif n in feeds:
+                value = feeds[n]
+            else:
                 raise WholePlanError(f"no feed supplied for const {n!r}")
-            a = np.ascontiguousarray(np.asarray(feeds[n]), dtype=_NP[p.dtype])
+            a = np.ascontiguousarray(np.asarray(value), dtype=_NP[p.dtype])
             if tuple(a.shape) != tuple(p.shape):
                 raise WholePlanError(f"feed {n!r} has shape {a.shape}, declared {p.shape}")
             raw = a.tobytes()

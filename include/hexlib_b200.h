@@ -94,6 +94,8 @@ extern "C" {
 #define HEXLIB_B200_KIND_ATTENTION        13  /* scale->QK^T->softmax->PV, fused */
 #define HEXLIB_B200_KIND_RMSNORM          14
 #define HEXLIB_B200_KIND_MATMUL_EPILOGUE_RESIDUAL 15 /* act(a@w+b) + r */
+#define HEXLIB_B200_KIND_MATMUL_EPILOGUE_ROPE 16 /* act(a@w+b), RoPE on heads */
+#define HEXLIB_B200_KIND_ATTENTION_QKV    17  /* attention over packed q|k|v */
 
 /* Invoke modes. */
 #define HEXLIB_B200_MODE_GRAPH   0u  /* capture once per blob, replay one graph  */
@@ -236,6 +238,22 @@ HEXLIB_B200_API int hexlib_b200_matmul_epilogue_residual_fp16(const void *a, con
                                               const void *r, void *out, int M,
                                               int K, int N, int act,
                                               void *stream);
+/* matmul_epilogue whose first `rope_cols` output columns are 64-wide heads
+ * rotated by the split-half 2-D RoPE of kernels/rope_2d_fp16/kernel_api.h
+ * (token of row r: r % T of the [T, 64] cos/sin tables), applied after the
+ * fp16 rounding exactly as rope_2d applies it to a stored q or k. With
+ * w = [wq | wk | wv] it is the whole q/k/v projection of a block
+ * (hexlib/models/vit.py:168-175) in one GEMM. */
+HEXLIB_B200_API int hexlib_b200_matmul_epilogue_rope_fp16(
+    const void *a, const void *w, const float *bias, const float *costab,
+    const float *sintab, void *out, int M, int K, int N, int act, int rope_cols,
+    int T, void *stream);
+/* Fused attention over a packed projection: qkv [B, T, 3, H, D] (the output
+ * of the call above), ctx [B, T, H, D] -- the layout the o-projection reads,
+ * so none of the block's four transposes is needed. D must be 64. */
+HEXLIB_B200_API int hexlib_b200_attention_qkv_fp16(const void *qkv, void *ctx,
+                                                   int B, int T, int H, int D,
+                                                   float scale, void *stream);
 /* Fused attention over Bn independent heads, q/k/v/ctx [Bn, T, D] fp16:
  * ctx = softmax((q*scale) @ k^T) @ v, the chain hexlib/models/vit.py:183-190
  * writes as five ops, without materialising the [Bn, T, T] scores. */

@@ -1,0 +1,91 @@
+"""The packed q/k/v path: one GEMM over [wq|wk|wv] with RoPE in its epilogue,
+attention straight from the packed [T, 3, H, D] tensor into [T, H, D]."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from hexlib_b200 import feeds as F
+from hexlib_b200 import graph as G
+from hexlib_b200 import wholeplan
+from hexlib_b200.session import Session
+from oracle import executor, ops
+from tests import gpu_util as U
+from tests.tolerance import assert_close_f16
+
+pytestmark = pytest.mark.gpu
+
+
+def r16(shape, seed, scale=1.0):
+    return (np.random.default_rng(seed).standard_normal(shape) * scale).astype(np.float16)
+
+
+@pytest.mark.parametrize("T,H,n_img", [(256, 12, 2), (64, 4, 3), (1024, 12, 1)])
+def test_rope_gemm_equals_three_projections_then_rope(T, H, n_img):
+    D, K = 64, H * 64
+    M = T * n_img
+    a = r16((M, K), 1)
+    ws = [r16((K, H * D), 2 + i, 0.05) for i in range(3)]
+    bs = [(np.random.default_rng(5 + i).standard_normal(H * D) * 0.02).astype(np.float32)
+          for i in range(3)]
+    ang = np.random.default_rng(9).uniform(-3, 3, (T, D)).astype(np.float32)
+    cos, sin = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+    w = np.concatenate(ws, 1)
+    b = np.concatenate(bs)
+    y = U.empty((M, 3 * H * D), np.float16)
+    da, dw, db, dc, ds = U.dev(a), U.dev(w), U.dev(b), U.dev(cos), U.dev(sin)
+    U.call("hexlib_b200_matmul_epilogue_rope_fp16", U.ptr(da), U.ptr(dw), U.ptr(db), U.ptr(dc),
+           U.ptr(ds), U.ptr(y), M, K, 3 * H * D, 0, 2 * H * D, T, U.stream())
+    got = U.host(y).reshape(n_img, T, 3, H, D)
+    af = a.astype(np.float32)
+    for i, which in enumerate("qkv"):
+        proj = ops.store(ops.matmul_epilogue((af, ws[i].astype(np.float32), bs[i]),
+                                             {"act": "none"})[0], "fp16")
+        proj = proj.reshape(n_img, T, H, D)
+        for n in range(n_img):
+            want = proj[n]
+            if which != "v":
+                want = ops.store(ops.rope_2d((want, cos, sin), {})[0], "fp16")
+            assert_close_f16(got[n, :, i], want, what=f"{which} image {n}")
+
+
+def exact(q, k, v, scale):
+    q, k, v = (x.astype(np.float64) for x in (q, k, v))
+    s = np.einsum("thd,shd->hts", q, k) * scale
+    p = np.exp(s - s.max(-1, keepdims=True))
+    p /= p.sum(-1, keepdims=True)
+    return np.einsum("hts,shd->thd", p, v).astype(np.float16).astype(np.float64)
+
+
+@pytest.mark.parametrize("B,T,H", [(2, 256, 12), (1, 1024, 12), (3, 200, 4), (2, 64, 2)])
+def test_attention_over_the_packed_projection(B, T, H):
+    qkv = r16((B, T, 3, H, 64), 11 + T)
+    ctx = U.empty((B, T, H, 64), np.float16)
+    d = U.dev(qkv)
+    U.call("hexlib_b200_attention_qkv_fp16", U.ptr(d), U.ptr(ctx), B, T, H, 64, 0.125, U.stream())
+    got = U.host(ctx)
+    for b in range(B):
+        want = exact(qkv[b, :, 0], qkv[b, :, 1], qkv[b, :, 2], 0.125)
+        assert_close_f16(got[b], want, what=f"image {b}")
+
+
+def test_packed_attention_refuses_what_it_cannot_serve():
+    assert U.call_rc("hexlib_b200_attention_qkv_fp16", 0, 0, 1, 64, 2, 32, 0.125, 0) == 6
+    assert U.call_rc("hexlib_b200_attention_qkv_fp16", 0, 0, 1, 64, 2, 64, -1.0, 0) == 6
+
+
+def test_fully_fused_encoder_matches_the_oracle():
+    cfg = G.qwen35_at(256)
+    g = G.build_vision_encoder(cfg)
+    w = F.weights(cfg, 0, g)
+    imgs = F.images(cfg, 2, 21)
+    ep = G.compile_for_cuda(g, residual=True, qkv=True)
+    plan = wholeplan.build_cuda_plan(ep, w, alias=True)
+    assert plan.kinds.count("attention_qkv") == 12
+    with Session(0) as s:
+        s.load(plan, max_images=2)
+        out = s.run(np.ascontiguousarray(imgs))
+    for i in range(2):
+        ref = executor.run(G.compile_for_cuda(g), dict(w, image=imgs[i]))["merger.out"]
+        err = np.abs(out[i].astype(np.float64) - ref).max() / np.abs(ref).max()
+        assert err < 1e-2, f"image {i}: relative error {err:.3e}"
