@@ -51,6 +51,7 @@ def parse():
     ap.add_argument("--batch", type=int, default=64, help="global batch (images)")
     ap.add_argument("--no-attention-fusion", action="store_true")
     ap.add_argument("--no-residual-fusion", action="store_true")
+    ap.add_argument("--no-qkv-fusion", action="store_true")
     return ap.parse_args()
 
 
@@ -213,6 +214,12 @@ def op_work(plan, op_index: int, n_images: int) -> tuple[str, float, str]:
         q = P[names[srcs[0]]]
         Bn, T, D = q.shape
         return "tensor", 4.0 * Bn * n_images * T * T * D, "FLOP"
+    if vname == "attention_qkv":
+        T, _, H, D = P[names[srcs[0]]].shape
+        return "tensor", 4.0 * H * n_images * T * T * D, "FLOP"
+    if vname == "matmul_epilogue_rope":
+        a, w = P[names[srcs[0]]], P[names[srcs[1]]]
+        return "tensor", 2.0 * a.shape[0] * n_images * w.shape[0] * w.shape[1], "FLOP"
     return "hbm", float(sum(nb(s) for s in srcs) + sum(nb(d) for d in dsts)), "B"
 
 
@@ -239,7 +246,9 @@ def run_b200(args) -> None:
     cfg = G.qwen35_at(args.image_size)
     g = G.build_vision_encoder(cfg)
     use_att = (not args.no_attention_fusion) and attention_available()
-    ep = G.compile_for_cuda(g, attention=use_att, residual=not args.no_residual_fusion)
+    use_qkv = use_att and not args.no_qkv_fusion
+    ep = G.compile_for_cuda(g, attention=use_att, residual=not args.no_residual_fusion,
+                            qkv=use_qkv)
     w = F.weights(cfg, 0, g)
     plan = wholeplan.build_cuda_plan(ep, w, alias=True)
     sh = D.shard(args.batch, rank, world)
@@ -362,7 +371,7 @@ def run_b200(args) -> None:
                             f"global batch {args.batch}, sharded by image",
                 "image_size": cfg.image_size, "global_batch": args.batch,
                 "seq_len": cfg.num_tokens, "parallelism": f"image-sharded x{world}",
-                "plan_ops": plan.n_ops, "fusions": {"attention": use_att,
+                "plan_ops": plan.n_ops, "fusions": {"attention": use_att, "qkv_rope": use_qkv,
                                                    "residual": not args.no_residual_fusion},
                 "l2": "inputs larger than L2: each step reads 201 MB of weights and "
                       f"{n * 6.29:.0f} MB of images per GPU",

@@ -356,6 +356,22 @@ int check_op(const OpRec& op) {
         return HEXLIB_B200_ERR_INVAL_PARAMS;
       return HEXLIB_B200_OK;
     }
+    case HEXLIB_B200_KIND_ROPE_QK: {
+      HB_TRY(need(op, 4));
+      HB_TRY(dt(op, 0, DT_FP16));
+      HB_TRY(dt(op, 1, DT_FP32));
+      HB_TRY(dt(op, 2, DT_FP32));
+      HB_TRY(dt(op, 3, DT_FP16));
+      HB_TRY(batching(op, 3));
+      const uint32_t* x = op.a[0].ne;   // T, 3, H, D
+      const uint32_t* c = op.a[1].ne;   // T, D
+      if (x[1] != 3 || x[0] == 0 || x[2] == 0 || x[3] == 0 || x[3] % 16 ||
+          memcmp(op.a[3].ne, x, sizeof(uint32_t) * 4) != 0 ||
+          memcmp(op.a[2].ne, c, sizeof(uint32_t) * 4) != 0 || c[0] != x[0] ||
+          c[1] != x[3] || c[2] != 1 || c[3] != 1 || op.a[1].per_image || op.a[2].per_image)
+        return HEXLIB_B200_ERR_INVAL_PARAMS;
+      return HEXLIB_B200_OK;
+    }
     case HEXLIB_B200_KIND_ATTENTION_QKV: {
       HB_TRY(need(op, 2));
       HB_TRY(dt(op, 0, DT_FP16));
@@ -500,6 +516,10 @@ int run_op(const OpRec& op, uint32_t n_images, int* err, cudaStream_t s) {
       g.rope_cols = op.params[1];
       return hb::launch_gemm(g, err, s);
     }
+    case HEXLIB_B200_KIND_ROPE_QK:
+      return hb::launch_rope_qk_f16(a[0].ptr, (const float*)a[1].ptr, (const float*)a[2].ptr,
+                                    a[3].ptr, (int64_t)a[0].ne[0] * B, (int)a[0].ne[2],
+                                    (int)a[0].ne[3], (int64_t)a[1].ne[0], s);
     case HEXLIB_B200_KIND_ATTENTION_QKV:
       return hb::launch_attention_qkv(a[0].ptr, a[1].ptr, B, (int)a[0].ne[0], (int)a[0].ne[2],
                                       (int)a[0].ne[3], param_f(op, 0), err, s);

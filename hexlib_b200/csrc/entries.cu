@@ -238,6 +238,14 @@ int hexlib_b200_matmul_epilogue_rope_fp16(const void* a, const void* w, const fl
   return hb::launch_gemm(g, hb::default_error_word(), as_stream(stream));
 }
 
+int hexlib_b200_rope_qk_fp16(const void* qkv, const float* costab, const float* sintab,
+                             void* out, int rows, int H, int D, int T, void* stream) {
+  HB_ENTRY_INIT();
+  if (rows < 0 || T <= 0 || !qkv || !out || !costab || !sintab)
+    return HEXLIB_B200_ERR_INVAL_PARAMS;
+  return hb::launch_rope_qk_f16(qkv, costab, sintab, out, rows, H, D, T, as_stream(stream));
+}
+
 int hexlib_b200_attention_qkv_fp16(const void* qkv, void* ctx, int B, int T, int H, int D,
                                    float scale, void* stream) {
   HB_ENTRY_INIT();

@@ -40,6 +40,11 @@ int launch_rope_f16(const void* x, const float* cos_t, const float* sin_t,
                     void* y, int64_t rows, int H, int D, int64_t table_rows,
                     cudaStream_t s);
 
+// RoPE on the q and k sections of a packed [rows, 3, H, D] projection; out
+// may equal qkv (in place), otherwise the whole tensor is copied first.
+int launch_rope_qk_f16(const void* qkv, const float* cos_t, const float* sin_t, void* out,
+                       int64_t rows, int H, int D, int64_t table_rows, cudaStream_t s);
+
 // Layout moves. `nimg` independent [T,H,D] -> [H,T,D] permutes.
 int launch_transpose_th_f16(const void* x, void* y, int64_t nimg, int T, int H,
                             int D, cudaStream_t s);

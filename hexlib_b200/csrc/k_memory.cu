@@ -505,6 +505,60 @@ __global__ void rope_f16_scalar(const __half* __restrict__ x,
   }
 }
 
+// ---- rope over the packed projection, in place -------------------------------------
+// qkv is [rows, 3, H, D]; the q and k sections (0 and 1) of every row are
+// rotated exactly as rope_f16_vec rotates a [T, H, D] tensor, the v section is
+// untouched. Each thread reads the 16 bytes it later writes, so x == y is safe.
+__global__ void rope_qk_vec(const uint4* x, const float* __restrict__ cos_t,
+                            const float* __restrict__ sin_t, uint4* y, int64_t rows,
+                            int H, int D, int64_t table_rows) {
+  const int half = D >> 1;
+  const int cpr = half >> 3;                       // 8-wide chunks per half
+  const int64_t per_row = 2LL * H * cpr;           // q and k heads
+  const int64_t total = rows * per_row;
+  const int64_t row_elems = 3LL * H * D;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = i / per_row;
+    const int rem = (int)(i - row * per_row);
+    const int c = rem % cpr;
+    const int sh = rem / cpr;                      // section * H + head, section < 2
+    const int64_t tt = row % table_rows;
+    const int64_t base = row * row_elems + (int64_t)sh * D;
+    const int i0 = c * 8;
+    H8 lo, hi, olo, ohi;
+    lo.u = x[(base + i0) / 8];
+    hi.u = x[(base + half + i0) / 8];
+    const float* ct = cos_t + tt * D;
+    const float* st = sin_t + tt * D;
+    const float4 c0 = __ldg(reinterpret_cast<const float4*>(ct + i0));
+    const float4 c1 = __ldg(reinterpret_cast<const float4*>(ct + i0 + 4));
+    const float4 c2 = __ldg(reinterpret_cast<const float4*>(ct + half + i0));
+    const float4 c3 = __ldg(reinterpret_cast<const float4*>(ct + half + i0 + 4));
+    const float4 s0 = __ldg(reinterpret_cast<const float4*>(st + i0));
+    const float4 s1 = __ldg(reinterpret_cast<const float4*>(st + i0 + 4));
+    const float4 s2 = __ldg(reinterpret_cast<const float4*>(st + half + i0));
+    const float4 s3 = __ldg(reinterpret_cast<const float4*>(st + half + i0 + 4));
+    const float cl[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    const float ch[8] = {c2.x, c2.y, c2.z, c2.w, c3.x, c3.y, c3.z, c3.w};
+    const float sl[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    const float sh8[8] = {s2.x, s2.y, s2.z, s2.w, s3.x, s3.y, s3.z, s3.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 a = __half22float2(lo.h2[q]);
+      const float2 b = __half22float2(hi.h2[q]);
+      const float ylo0 = __fadd_rn(__fmul_rn(a.x, cl[2 * q]), __fmul_rn(-b.x, sl[2 * q]));
+      const float ylo1 = __fadd_rn(__fmul_rn(a.y, cl[2 * q + 1]), __fmul_rn(-b.y, sl[2 * q + 1]));
+      const float yhi0 = __fadd_rn(__fmul_rn(b.x, ch[2 * q]), __fmul_rn(a.x, sh8[2 * q]));
+      const float yhi1 = __fadd_rn(__fmul_rn(b.y, ch[2 * q + 1]), __fmul_rn(a.y, sh8[2 * q + 1]));
+      olo.h2[q] = __floats2half2_rn(ylo0, ylo1);
+      ohi.h2[q] = __floats2half2_rn(yhi0, yhi1);
+    }
+    y[(base + i0) / 8] = olo.u;
+    y[(base + half + i0) / 8] = ohi.u;
+  }
+}
+
 // ---- transpose_th: [T,H,D] -> [H,T,D] per image ----------------------------------
 // D is innermost on both sides, so the op moves whole D-runs: one thread per
 // 16-byte vector, coalesced on both sides.
@@ -681,6 +735,7 @@ int memory_kernels_init() {
       (const void*)softmax_f16_reg<8>,  (const void*)softmax_f16_reg<16>,
       (const void*)softmax_f16_generic, (const void*)rope_f16_vec,
       (const void*)rope_f16_scalar,     (const void*)transpose_th_vec,
+      (const void*)rope_qk_vec,
       (const void*)transpose_th_scalar, (const void*)transpose_hd_tiled,
       (const void*)patchify_vec,        (const void*)patchify_scalar,
   };
@@ -874,6 +929,23 @@ int launch_rope_f16(const void* x, const float* cos_t, const float* sin_t,
     rope_f16_scalar<<<grid_for(total, kThreads), kThreads, 0, s>>>(
         (const __half*)x, cos_t, sin_t, (__half*)y, rows, H, D, table_rows);
   }
+  HB_LAUNCH_CHECK();
+}
+
+int launch_rope_qk_f16(const void* qkv, const float* cos_t, const float* sin_t, void* out,
+                       int64_t rows, int H, int D, int64_t table_rows, cudaStream_t s) {
+  if (rows < 0 || H <= 0 || D <= 0 || (D % 16) || table_rows <= 0)
+    return HEXLIB_B200_ERR_INVAL_PARAMS;
+  if (rows == 0) return HEXLIB_B200_OK;
+  if (!aligned16(qkv) || !aligned16(out) || !aligned16(cos_t) || !aligned16(sin_t))
+    return HEXLIB_B200_ERR_INVAL_PARAMS;
+  if (qkv != out) {  // not in place: carry the v section over first
+    const int rc = launch_copy(qkv, out, rows * 3LL * H * D * 2, s);
+    if (rc != HEXLIB_B200_OK) return rc;
+  }
+  const int64_t total = rows * 2LL * H * (D / 16);
+  rope_qk_vec<<<grid_for(total, kThreads), kThreads, 0, s>>>(
+      (const uint4*)out, cos_t, sin_t, (uint4*)out, rows, H, D, table_rows);
   HB_LAUNCH_CHECK();
 }
 

@@ -464,8 +464,9 @@ def fuse_qkv(graph: Graph) -> tuple[Graph, dict[str, tuple]]:
     rope_2d of q and k, the three [T,H,D] -> [H,T,D] transposes into the
     attention op and the transpose of its output back to [T, H, D] become
 
-        qkv   = matmul_epilogue_rope(a, [wq|wk|wv], [bq|bk|bv], cos, sin)  [T, 3, H, D]
-        ctx.t = attention_qkv(qkv)                                         [T, H, D]
+        raw   = matmul_epilogue(a, [wq|wk|wv], [bq|bk|bv])   [T, 3, H, D]
+        qkv   = rope_qk(raw, cos, sin)                       [T, 3, H, D]  (in place)
+        ctx.t = attention_qkv(qkv)                           [T, H, D]
 
     The concatenated weight and bias are new consts, returned as
     `{name: ("concat", (parts...), axis)}` for the batch builder to derive from
@@ -535,14 +536,18 @@ def fuse_qkv(graph: Graph) -> tuple[Graph, dict[str, tuple]]:
             continue
         wname = f"concat({ws[0]},{ws[1]},{ws[2]})"
         bname = f"concat({bs[0]},{bs[1]},{bs[2]})"
+        raw = f"{mms[0].outputs[0]}+qkv.raw"
         qkv = f"{mms[0].outputs[0]}+qkv"
         new_tensors[wname] = Tensor(wname, "fp16", (K, 3 * heads * d), True)
         new_tensors[bname] = Tensor(bname, "fp32", (3 * heads * d,), True)
+        new_tensors[raw] = Tensor(raw, "fp16", (n_tok, 3, heads, d), False)
         new_tensors[qkv] = Tensor(qkv, "fp16", (n_tok, 3, heads, d), False)
         derived[wname] = ("concat", tuple(ws), 1)
         derived[bname] = ("concat", tuple(bs), 0)
-        rewritten[mms[0].id] = Op(mms[0].id, "matmul_epilogue_rope", (a, wname, bname, cos, sin),
-                                  (qkv,), {"act": "none", "rope_cols": 2 * heads * d})
+        rewritten[mms[0].id] = Op(mms[0].id, "matmul_epilogue", (a, wname, bname), (raw,),
+                                  {"act": "none"})
+        # the rope takes the k projection's op id, free once that op is gone
+        rewritten[mms[1].id] = Op(mms[1].id, "rope_qk", (raw, cos, sin), (qkv,), {})
         rewritten[ctx_t.id] = Op(ctx_t.id, "attention_qkv", (qkv,), ctx_t.outputs,
                                  {"scale": float(att.attrs["scale"])})
         for w in "qkv":
@@ -554,6 +559,7 @@ def fuse_qkv(graph: Graph) -> tuple[Graph, dict[str, tuple]]:
         consumed.add(att.id)
         dropped.add(att.outputs[0])
         consumed.discard(mms[0].id)
+        consumed.discard(mms[1].id)
     if not rewritten:
         return graph, {}
     ops = tuple(rewritten.get(o.id, o) for o in graph.ops

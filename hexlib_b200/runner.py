@@ -18,8 +18,8 @@ DIFFERENCES FROM THE DSP's TABLE, each deliberate:
   * reshape has a variant (a device copy): the batch builder still elides
     reshapes by aliasing, but a blob that carries one is served.
   * ids are appended for kernels the DSP table does not have: attention (13),
-    rmsnorm (14), matmul_epilogue_residual (15), matmul_epilogue_rope (16)
-    and attention_qkv (17).
+    rmsnorm (14), matmul_epilogue_residual (15), matmul_epilogue_rope (16),
+    attention_qkv (17) and rope_qk (18).
 """
 from __future__ import annotations
 
@@ -46,6 +46,7 @@ KIND_ID: dict[str, int] = {
     "matmul_epilogue_residual": 15,
     "matmul_epilogue_rope": 16,
     "attention_qkv": 17,
+    "rope_qk": 18,
 }
 
 ACT_CODES = (("none", 0), ("gelu_tanh", 1), ("gelu_erf", 2))
@@ -148,6 +149,7 @@ SPECS: dict[str, CudaSpec] = {
         "matmul_epilogue_rope", (F16, F16, F32, F32, F32), "fp16",
         params=(Param("act", "int", ACT_CODES), Param("rope_cols")),
         entry="hexlib_b200_matmul_epilogue_rope_fp16"),
+    "rope_qk": CudaSpec("rope_qk", (F16, F32, F32), "fp16", entry="hexlib_b200_rope_qk_fp16"),
     "attention_qkv": CudaSpec("attention_qkv", (F16,), "fp16",
                               params=(Param("scale", "float"),),
                               entry="hexlib_b200_attention_qkv_fp16"),

@@ -37,6 +37,11 @@ ALIGN = 256
 
 _NP = {"fp32": np.float32, "fp16": np.float16, "int32": np.int32}
 
+# kinds whose output may share its first input's storage: their kernels read
+# each element before writing it, and the rewrite that emits them leaves the
+# input with no other consumer (checked below)
+INPLACE_KINDS = frozenset({"rope_qk"})
+
 
 class WholePlanError(Exception):
     pass
@@ -120,10 +125,21 @@ def build_cuda_plan(compiled, feeds: Mapping[str, Any] | None = None,
     io_names = set(graph.inputs) | set(graph.outputs)
     const_names = {n for n, t in tensors.items() if t.const}
 
+    # Outputs stored on their input's bytes: reshape (a reinterpretation) and
+    # the in-place kinds, whose kernels read every element before writing it.
     reshape_src: dict[str, str] = {}
     for op in order:
-        if op.kind == "reshape":
+        if op.kind == "reshape" or op.kind in INPLACE_KINDS:
             reshape_src[op.outputs[0]] = op.inputs[0]
+
+    for i, op in enumerate(order):
+        if op.kind in INPLACE_KINDS:
+            src = op.inputs[0]
+            later = [o.id for o in order[i + 1:] if src in o.inputs]
+            if later or src in io_names:
+                raise WholePlanError(
+                    f"op {op.id} ({op.kind}) would overwrite {src!r}, which ops {later} "
+                    "still read (or the host reads); it cannot run in place")
 
     def owner(name: str) -> str:
         seen = {name}

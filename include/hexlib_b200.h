@@ -96,6 +96,7 @@ extern "C" {
 #define HEXLIB_B200_KIND_MATMUL_EPILOGUE_RESIDUAL 15 /* act(a@w+b) + r */
 #define HEXLIB_B200_KIND_MATMUL_EPILOGUE_ROPE 16 /* act(a@w+b), RoPE on heads */
 #define HEXLIB_B200_KIND_ATTENTION_QKV    17  /* attention over packed q|k|v */
+#define HEXLIB_B200_KIND_ROPE_QK          18  /* rope_2d of the q, k sections */
 
 /* Invoke modes. */
 #define HEXLIB_B200_MODE_GRAPH   0u  /* capture once per blob, replay one graph  */
@@ -248,6 +249,13 @@ HEXLIB_B200_API int hexlib_b200_matmul_epilogue_rope_fp16(
     const void *a, const void *w, const float *bias, const float *costab,
     const float *sintab, void *out, int M, int K, int N, int act, int rope_cols,
     int T, void *stream);
+/* rope_2d (kernels/rope_2d_fp16/kernel_api.h:120-121) applied to the q and
+ * k sections of a packed [rows, 3, H, D] projection, token of row r = r % T
+ * of the [T, D] tables; the v section is left as it is. out may equal qkv
+ * (in place). */
+HEXLIB_B200_API int hexlib_b200_rope_qk_fp16(const void *qkv, const float *costab,
+                                             const float *sintab, void *out, int rows,
+                                             int H, int D, int T, void *stream);
 /* Fused attention over a packed projection: qkv [B, T, 3, H, D] (the output
  * of the call above), ctx [B, T, H, D] -- the layout the o-projection reads,
  * so none of the block's four transposes is needed. D must be 64. */

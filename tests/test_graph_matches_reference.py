@@ -105,17 +105,17 @@ def test_invalid_configs_are_refused():
 def test_qkv_rewrite_packs_the_projections_and_drops_the_transposes():
     ep = G.compile_for_cuda(G.build_vision_encoder(G.qwen35_at(256)), residual=True, qkv=True)
     c = Counter(o.kind for o in ep.graph.ops)
-    assert c["matmul_epilogue_rope"] == 12 and c["attention_qkv"] == 12
+    assert c["rope_qk"] == 12 and c["attention_qkv"] == 12
     assert c["transpose"] == 0 and c["rope_2d"] == 0 and c["attention"] == 0
-    assert c["matmul_epilogue"] == 12 + 3    # fc1 per block; patch embed, merger fc1/fc2
+    # qkv and fc1 per block; patch embed, merger fc1/fc2
+    assert c["matmul_epilogue"] == 12 + 12 + 3
     assert len(ep.derived) == 24
     for o in ep.graph.ops:
-        if o.kind == "matmul_epilogue_rope":
-            w = ep.graph.tensors[o.inputs[1]]
-            assert w.shape == (768, 2304) and w.const
-            assert o.attrs["rope_cols"] == 1536
+        if o.kind == "matmul_epilogue" and ep.graph.tensors[o.inputs[1]].shape == (768, 2304):
             how, parts, axis = ep.derived[o.inputs[1]]
             assert how == "concat" and axis == 1 and len(parts) == 3
+            assert ep.graph.tensors[o.outputs[0]].shape == (256, 3, 12, 64)
+        if o.kind == "rope_qk":
             assert ep.graph.tensors[o.outputs[0]].shape == (256, 3, 12, 64)
         if o.kind == "attention_qkv":
             assert ep.graph.tensors[o.outputs[0]].shape == (256, 12, 64)

@@ -11,7 +11,7 @@ from hexlib_b200 import wholeplan
 from hexlib_b200.session import Session
 from oracle import executor, ops
 from tests import gpu_util as U
-from tests.tolerance import assert_close_f16
+from tests.tolerance import assert_close_f16, f16_ulp
 
 pytestmark = pytest.mark.gpu
 
@@ -43,10 +43,40 @@ def test_rope_gemm_equals_three_projections_then_rope(T, H, n_img):
                                              {"act": "none"})[0], "fp16")
         proj = proj.reshape(n_img, T, H, D)
         for n in range(n_img):
-            want = proj[n]
-            if which != "v":
-                want = ops.store(ops.rope_2d((want, cos, sin), {})[0], "fp16")
-            assert_close_f16(got[n, :, i], want, what=f"{which} image {n}")
+            if which == "v":
+                assert_close_f16(got[n, :, i], proj[n], what=f"v image {n}")
+                continue
+            want = ops.store(ops.rope_2d((proj[n], cos, sin), {})[0], "fp16")
+            # y = x*cos -/+ partner*sin: each of the two GEMM outputs may sit one
+            # fp16 step from the oracle's fp32 summation order, and y is rounded
+            # once more -- the bound is those steps, weighted as the rotation does.
+            partner = np.concatenate([proj[n][..., D // 2:], proj[n][..., :D // 2]], -1)
+            bound = (f16_ulp(proj[n]) * np.abs(cos)[:, None, :]
+                     + f16_ulp(partner) * np.abs(sin)[:, None, :] + f16_ulp(want))
+            err = np.abs(got[n, :, i].astype(np.float64) - want)
+            assert np.all(err <= np.maximum(2e-3, bound)), \
+                f"{which} image {n}: worst excess {np.max(err - np.maximum(2e-3, bound)):.3e}"
+            assert np.mean(err == 0) > 0.99
+
+
+@pytest.mark.parametrize("inplace", [True, False])
+@pytest.mark.parametrize("T,H,n_img", [(256, 12, 2), (64, 4, 1)])
+def test_rope_qk_rotates_q_and_k_sections_only(T, H, n_img, inplace):
+    D = 64
+    qkv = r16((n_img, T, 3, H, D), 31)
+    ang = np.random.default_rng(33).uniform(-3, 3, (T, D)).astype(np.float32)
+    cos, sin = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+    d, dc, ds = U.dev(qkv), U.dev(cos), U.dev(sin)
+    out = d if inplace else U.empty(qkv.shape, np.float16)
+    U.call("hexlib_b200_rope_qk_fp16", U.ptr(d), U.ptr(dc), U.ptr(ds), U.ptr(out),
+           n_img * T, H, D, T, U.stream())
+    got = U.host(out)
+    for n in range(n_img):
+        for sec in range(2):
+            want = ops.store(ops.rope_2d((qkv[n, :, sec].astype(np.float32), cos, sin), {})[0],
+                             "fp16").astype(np.float16)
+            np.testing.assert_array_equal(got[n, :, sec], want)
+        np.testing.assert_array_equal(got[n, :, 2], qkv[n, :, 2])
 
 
 def exact(q, k, v, scale):
