@@ -10,10 +10,11 @@ collective. One step = the whole encoder over the whole batch.
 
   value    images/s of the whole job, device-timed with CUDA events on the
            session stream, inputs resident in HBM, max over ranks.
-  e2e      the same through the public API (Session.run): per step, the
-           host->device copy of the step's images from pinned memory, the
-           plan, the device->host copy of the embeddings (and the all-gather
-           for N > 1).
+  e2e      the same through the public API (session.Pipeline over two
+           sessions): per step, the host->device copy of the step's images
+           from pinned memory, the plan, the device->host copy of the
+           embeddings (and the all-gather for N > 1); one step's copies
+           overlap the other session's kernels.
   roofline the dominant kernel (largest share of one eager, op-by-op timed
            pass): algorithmic FLOPs or bytes per launch / its mean CUDA-event
            duration, against MEASURED_PEAKS.json.
@@ -44,7 +45,7 @@ UNIT = "images/s"
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--image-size", type=int, default=512)
@@ -138,9 +139,13 @@ class ClockSampler:
     def __init__(self, index: int):
         self.index = index
         self.proc = None
-        self.lines: list[str] = []
+        self.lines: list[tuple[float, str]] = []
+        self.windows: list[tuple[float, float]] = []
+        self._t0 = None
 
     def start(self):
+        """Start sampling every 100 ms and wait for the first sample, so the
+        timed windows that follow are covered from their first moment."""
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -148,12 +153,23 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            t_end = time.monotonic() + 10.0
+            while not self.lines and time.monotonic() < t_end and self.proc.poll() is None:
+                time.sleep(0.05)
         except Exception:  # noqa: BLE001
             self.proc = None
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.monotonic(), line.strip()))
+
+    def begin(self):
+        self._t0 = time.monotonic()
+
+    def end(self):
+        if self._t0 is not None:
+            self.windows.append((self._t0, time.monotonic()))
+            self._t0 = None
 
     def stop(self) -> dict:
         if self.proc is None:
@@ -165,7 +181,11 @@ class ClockSampler:
             self.proc.kill()
         sm, mx, reasons = [], None, set()
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for ln in self.lines:
+        # samples taken inside a timed window (one sampling period of slack at its end)
+        inside = [ln for t, ln in self.lines
+                  if any(a <= t <= e + 0.1 for a, e in self.windows)] if self.windows else \
+                 [ln for _, ln in self.lines]
+        for ln in inside:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -231,7 +251,7 @@ def run_b200(args) -> None:
     from hexlib_b200 import feeds as F
     from hexlib_b200 import graph as G
     from hexlib_b200 import wholeplan
-    from hexlib_b200.session import MODE_EAGER, Session, attention_available
+    from hexlib_b200.session import MODE_EAGER, Pipeline, Session, attention_available
 
     rank, local, world = D.env_rank()
     torch.cuda.set_device(local)
@@ -276,43 +296,73 @@ def run_b200(args) -> None:
         torch.cuda.synchronize()
         s.sync()
 
+    clocks = ClockSampler(local)
+    clocks.start()
     warm = max(args.warmup, 3)
     for _ in range(warm):
         step_device()
     s.sync()
 
     # ---- device-timed, inputs resident ----------------------------------------------
-    clocks = ClockSampler(local)
-    clocks.start()
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
+    clocks.begin()
     e0.record(stream)
     for _ in range(args.steps):
         step_device()
     e1.record(stream)
     s.sync()
     e1.synchronize()
+    clocks.end()
     ms = e0.elapsed_time(e1)
-    clk = clocks.stop()
     t = torch.tensor([ms], device="cuda")
     if pg is not None:
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
     ms_max = float(t.item())
     value = args.batch * args.steps / (ms_max / 1e3)
 
-    # ---- end to end through Session.run (pinned host buffers) ---------------------
+    # ---- end to end through the public Pipeline API (pinned host buffers) ----------
+    # Two sessions used in turn: each step uploads its images, replays the
+    # plan and reads its embeddings back on its own stream, so step k+1's
+    # upload overlaps step k's kernels. Every step's copies are inside the
+    # timed region, which runs from before the first upload to after the
+    # last read-back on every stream.
+    pipe = Pipeline(plan, max_images=n, device=local, sessions=[s])
+    dev = torch.device("cuda", local)
+    streams = [torch.cuda.ExternalStream(x.stream(), device=dev) for x in pipe.sessions]
+    views = [x.device_view(plan.outputs[0], n) for x in pipe.sessions]
+    host_outs = [host_out] + [torch.empty_like(host_out).pin_memory()
+                              for _ in pipe.sessions[1:]]
+
+    def step_e2e(k):
+        j = k % len(pipe.sessions)
+        pipe.submit(host_in, host_outs[j])
+        if pg is not None:
+            with torch.cuda.stream(streams[j]):
+                D.gather_embeddings(views[j])
+
+    for k in range(len(pipe.sessions)):      # the new session captures its graph
+        step_e2e(k)
+    pipe.drain()
     barrier()
     e2 = torch.cuda.Event(enable_timing=True)
     e3 = torch.cuda.Event(enable_timing=True)
-    e2.record(stream)
-    for _ in range(args.steps):
-        s.run(host_in, out=host_out.numpy())
-        if pg is not None:
-            with torch.cuda.stream(stream):
-                D.gather_embeddings(emb)
-    e3.record(stream)
+    clocks.begin()
+    e2.record(streams[0])
+    for st in streams[1:]:
+        st.wait_event(e2)
+    for k in range(args.steps):
+        step_e2e(k)
+    for st in streams[1:]:
+        ev = torch.cuda.Event()
+        ev.record(st)
+        streams[0].wait_event(ev)
+    e3.record(streams[0])
     e3.synchronize()
+    clocks.end()
+    clk = clocks.stop()
+    pipe.drain()
     ms_e2e = e2.elapsed_time(e3)
     t = torch.tensor([ms_e2e], device="cuda")
     if pg is not None:
@@ -390,6 +440,7 @@ def run_b200(args) -> None:
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
+    pipe.close()
     s.close()
     if pg is not None:
         pg.barrier()

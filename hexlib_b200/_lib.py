@@ -33,6 +33,8 @@ _PROTOS: dict[str, list] = {
     "hexlib_b200_munmap": [c_vp, c_u32],
     "hexlib_b200_buf_write": [c_vp, c_u32, c_u64, c_vp, c_u64],
     "hexlib_b200_buf_read": [c_vp, c_u32, c_u64, c_vp, c_u64],
+    "hexlib_b200_buf_write_async": [c_vp, c_u32, c_u64, c_vp, c_u64],
+    "hexlib_b200_buf_read_async": [c_vp, c_u32, c_u64, c_vp, c_u64],
     "hexlib_b200_buf_device_ptr": [c_vp, c_u32, ctypes.POINTER(c_u64),
                                    ctypes.POINTER(c_u64)],
     "hexlib_b200_stream": [c_vp, ctypes.POINTER(c_vp)],

@@ -980,6 +980,33 @@ int hexlib_b200_buf_read(hexlib_b200_ctx* ctx, uint32_t fd, uint64_t offset,
   return HEXLIB_B200_OK;
 }
 
+static int buf_copy_async(hexlib_b200_ctx* ctx, uint32_t fd, uint64_t offset, void* host,
+                          uint64_t nbytes, bool to_device) {
+  char* p = nullptr;
+  const int rc = buf_range(ctx, fd, offset, nbytes, &p);
+  if (rc != HEXLIB_B200_OK) return rc;
+  if (nbytes == 0) return HEXLIB_B200_OK;
+  if (!host) return HEXLIB_B200_ERR_INVAL_PARAMS;
+  const cudaError_t e =
+      to_device ? cudaMemcpyAsync(p, host, nbytes, cudaMemcpyHostToDevice, ctx->stream)
+                : cudaMemcpyAsync(host, p, nbytes, cudaMemcpyDeviceToHost, ctx->stream);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return HEXLIB_B200_ERR_CUDA;
+  }
+  return HEXLIB_B200_OK;
+}
+
+int hexlib_b200_buf_write_async(hexlib_b200_ctx* ctx, uint32_t fd, uint64_t offset,
+                                const void* src, uint64_t nbytes) {
+  return buf_copy_async(ctx, fd, offset, const_cast<void*>(src), nbytes, true);
+}
+
+int hexlib_b200_buf_read_async(hexlib_b200_ctx* ctx, uint32_t fd, uint64_t offset, void* dst,
+                               uint64_t nbytes) {
+  return buf_copy_async(ctx, fd, offset, dst, nbytes, false);
+}
+
 int hexlib_b200_buf_device_ptr(hexlib_b200_ctx* ctx, uint32_t fd, uint64_t* ptr,
                                uint64_t* alloc_bytes) {
   if (!ctx) return HEXLIB_B200_ERR_NOT_STARTED;

@@ -98,7 +98,83 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   return mbar_wait_limit(bar, parity, abort_flag, err, HB_WAIT_LIMIT_NS);
 }
 
+// ---- CTA pairs (clusters of two; see gemm_f16_pair) ------------------------
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Every thread of both CTAs; release/acquire orders the shared-memory writes
+// (barrier initialisation included) of each CTA before the other's reads.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Address of the same shared-memory object in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+  uint32_t a;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(p)), "r"(rank));
+  return a;
+}
+
+__device__ __forceinline__ void st_cluster_u32(uint32_t caddr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(caddr), "r"(v) : "memory");
+}
+
+// Arrive on an mbarrier that may live in the other CTA of the pair.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t caddr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(caddr)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// mbar_wait with cluster-scope acquire, for barriers arrived on from the
+// other CTA of a pair. Same limit and abort protocol as mbar_wait_limit.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
+                                                  volatile int* abort_flag, int* err) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  uint32_t n = 0;
+  while (true) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((++n & 63u) == 0) {
+      if (*abort_flag) return false;
+      if (global_timer_ns() - t0 > HB_WAIT_LIMIT_NS) {
+        *abort_flag = 1;
+        if (err) atomicExch(err, HB_DEVERR_WAIT_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+
 // ---- TMA (no multicast anywhere in this project) ---------------------------
+
+// Pair form: the tile lands in THIS CTA's shared memory and its bytes are
+// counted on the mbarrier at cluster address `bar_caddr`, which may be the
+// leader CTA's.
+__device__ __forceinline__ void tma_load_3d_pair(const CUtensorMap* map, uint32_t bar_caddr,
+                                                 void* smem_dst, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::"
+      "bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(map), "r"(bar_caddr), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
@@ -187,6 +263,52 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile(
       "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
       "[%0];" ::"r"(smem_u32(bar))
+      : "memory");
+}
+
+// ---- tcgen05, CTA-pair forms (cta_group::2) --------------------------------
+// Executed by the same warp in both CTAs of the pair; the two allocations get
+// the same TMEM address.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile(
+      "tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+          smem_u32(dst_smem)),
+      "r"(ncols)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr),
+               "r"(ncols)
+               : "memory");
+}
+
+// Issued by one thread of the leader CTA: M = 256 rows, 128 from each CTA's
+// A tile; N columns, N/2 from each CTA's B tile (same shared-memory offsets
+// in both); rows [0,128) accumulate in the leader's TMEM, [128,256) in the
+// other CTA's, at the same TMEM address.
+__device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t adesc,
+                                              uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(
+          d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum)
+      : "memory");
+}
+
+// When the pair MMAs issued so far have completed, arrive once on the
+// mbarrier at this shared-memory offset in each CTA named by `cta_mask`
+// (a tcgen05 completion signal -- not a data load).
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 "
+      "[%0], %1;" ::"r"(smem_u32(bar)),
+      "h"(cta_mask)
       : "memory");
 }
 

@@ -30,6 +30,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
 
 #include <mutex>
 
@@ -107,6 +108,117 @@ __device__ __forceinline__ void rope_head64(uint32_t (&lo)[16], uint32_t (&hi)[1
       const float z1 = __fadd_rn(__fmul_rn(b.y, ch[2 * q + 1]), __fmul_rn(a.y, sh[2 * q + 1]));
       lo[i + q] = pack_half2(y0, y1);
       hi[i + q] = pack_half2(z0, z1);
+    }
+  }
+}
+
+// One epilogue warp's share of a finished 128-row accumulator tile. TMEM
+// lanes [32*quarter, 32*quarter + 32) hold rows row0 + 32*quarter + lane of
+// batch entry b; the warp finishes the 64-column groups [g_lo, g_hi) of the
+// tile whose first column is n0: each group is read from TMEM 32 columns at a
+// time, finished in registers (bias, GELU, residual, rounding), written to
+// this warp's 128B-swizzled staging box and stored by one TMA store, which
+// also clips the tile's row and column tails.
+template <bool ROPE>
+__device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtensorMap* tmC,
+                                              uint32_t tacc, uint8_t* stage, int quarter,
+                                              int lane, int g_lo, int g_hi, int64_t b,
+                                              int64_t row0, int n0) {
+  const int64_t row = row0 + quarter * 32 + lane;
+  const bool row_ok = row < p.M;
+  const uint32_t trow = tacc + ((uint32_t)(quarter * 32) << 16);
+  const __half* rrow =
+      (p.resid && row_ok) ? p.resid + (b * p.M + row) * (int64_t)p.N : nullptr;
+  const int rl = lane;                                        // row within the slab
+#pragma unroll 1
+  for (int g = g_lo; g < g_hi; ++g) {
+    // the previous group's store must have finished reading the stage
+    if (lane == 0) bulk_wait_read_all();
+    __syncwarp();
+    uint32_t packed[2][16];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int c32 = g * 64 + h * 32;          // column within the tile
+      const int nc = n0 + c32;             // global column
+      // issue the global loads first so their latency overlaps the TMEM read
+      float bias[32];
+      if (p.bias && nc < p.N) {
+        const float4* bp = reinterpret_cast<const float4*>(p.bias + nc);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float4 bb = (nc + 4 * j < p.N) ? __ldg(bp + j) : make_float4(0, 0, 0, 0);
+          bias[4 * j] = bb.x; bias[4 * j + 1] = bb.y;
+          bias[4 * j + 2] = bb.z; bias[4 * j + 3] = bb.w;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) bias[j] = 0.f;
+      }
+      uint4 res[4];
+      if (rrow) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          res[j] = (nc + 8 * j < p.N) ? __ldg(reinterpret_cast<const uint4*>(rrow + nc) + j)
+                                      : make_uint4(0, 0, 0, 0);
+      }
+      uint32_t rg[32];
+      tmem_ld_32x32b_x32(trow + c32, rg);
+      tmem_ld_wait();
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(rg[j]) + bias[j];
+      if (p.act == 1) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = gelu_tanh_f(v[j]);
+      } else if (p.act == 2) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = gelu_erf_f(v[j]);
+      }
+      uint32_t hw[16];
+      if (rrow) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const __half2* rh = reinterpret_cast<const __half2*>(&res[j]);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            // The matmul result is an fp16 tensor in the unfused plan:
+            // round it, then add the residual in fp32 and round again.
+            const float2 fm = __half22float2(
+                __floats2half2_rn(v[8 * j + 2 * q], v[8 * j + 2 * q + 1]));
+            const float2 fr = __half22float2(rh[q]);
+            hw[4 * j + q] = pack_half2(fr.x + fm.x, fr.y + fm.y);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < 16; ++q) hw[q] = pack_half2(v[2 * q], v[2 * q + 1]);
+      }
+#pragma unroll
+      for (int q = 0; q < 16; ++q) packed[h][q] = hw[q];
+    }
+    if (ROPE) {
+      const int n64 = n0 + g * 64;
+      if (n64 < p.rope_cols && row_ok) {
+        const int tok = (int)(row % p.rope_T);
+        rope_head64(packed[0], packed[1], p.rope_cos + (int64_t)tok * 64,
+                    p.rope_sin + (int64_t)tok * 64);
+      }
+    }
+    // 8 x 16 B into the 128-byte row rl of the stage, swizzled
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int chunk = (h * 4 + j) ^ (rl & 7);
+        *reinterpret_cast<uint4*>(stage + rl * 128 + chunk * 16) =
+            make_uint4(packed[h][4 * j], packed[h][4 * j + 1], packed[h][4 * j + 2],
+                       packed[h][4 * j + 3]);
+      }
+    fence_proxy_async_shared();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_3d(tmC, stage, n0 + g * 64, (int)(row0 + quarter * 32), (int)b);
+      bulk_commit_group();
     }
   }
 }
@@ -227,20 +339,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
-    // Epilogue. Warp (quarter, colhalf) owns TMEM lanes [32q, 32q+32) -- rows
-    // of the tile -- and half of its columns, in groups of 64: each group is
-    // read from TMEM 32 columns at a time, finished in registers (bias, GELU,
-    // residual, rounding), written to this warp's 128B-swizzled staging box
-    // and stored to global memory by one TMA store, which also clips the
-    // tile's row and column tails.
+    // Epilogue: warp (quarter, colhalf) owns TMEM lanes [32q, 32q+32) -- rows
+    // of the tile -- and half of its 64-column groups.
     const int ew = warp - 2;
     const int quarter = warp & 3;
     const int colhalf = ew >> 2;
-    constexpr int kGroups = BN / 64;                          // 64-column groups
+    constexpr int kGroups = BN / 64;
     const int g_lo = (kGroups >= 2) ? colhalf * (kGroups / 2) : 0;
     const int g_hi = (kGroups >= 2) ? (colhalf + 1) * (kGroups / 2) : (colhalf ? 0 : 1);
     uint8_t* stage = sOut + ew * 4096;
-    const int rl = lane;                                      // row within the slab
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int64_t t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
@@ -249,107 +356,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int mb = (int)(r / p.tiles_n);
       const int nb = (int)(r % p.tiles_n);
       // Every lane waits; the warp proceeds only if all of them saw the
-      // phase complete, because tcgen05.ld below is warp-collective.
+      // phase complete, because tcgen05.ld is warp-collective.
       const bool ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, p.err);
       if (!__all_sync(0xffffffffu, ok)) goto done;
       tc_fence_after();
-      const int64_t row = (int64_t)mb * BM + quarter * 32 + lane;
-      const bool row_ok = row < p.M;
-      const uint32_t trow =
-          tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
-      const __half* rrow =
-          (p.resid && row_ok) ? p.resid + (b * p.M + row) * (int64_t)p.N : nullptr;
-#pragma unroll 1
-      for (int g = g_lo; g < g_hi; ++g) {
-        // the previous group's store must have finished reading the stage
-        if (lane == 0) bulk_wait_read_all();
-        __syncwarp();
-        uint32_t packed[2][16];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int c32 = g * 64 + h * 32;          // column within the tile
-          const int n0 = nb * BN + c32;             // global column
-          // issue the global loads first so their latency overlaps the TMEM read
-          float bias[32];
-          if (p.bias && n0 < p.N) {
-            const float4* bp = reinterpret_cast<const float4*>(p.bias + n0);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const float4 bb = (n0 + 4 * j < p.N) ? __ldg(bp + j) : make_float4(0, 0, 0, 0);
-              bias[4 * j] = bb.x; bias[4 * j + 1] = bb.y;
-              bias[4 * j + 2] = bb.z; bias[4 * j + 3] = bb.w;
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) bias[j] = 0.f;
-          }
-          uint4 res[4];
-          if (rrow) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              res[j] = (n0 + 8 * j < p.N) ? __ldg(reinterpret_cast<const uint4*>(rrow + n0) + j)
-                                          : make_uint4(0, 0, 0, 0);
-          }
-          uint32_t rg[32];
-          tmem_ld_32x32b_x32(trow + c32, rg);
-          tmem_ld_wait();
-          float v[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(rg[j]) + bias[j];
-          if (p.act == 1) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = gelu_tanh_f(v[j]);
-          } else if (p.act == 2) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = gelu_erf_f(v[j]);
-          }
-          uint32_t hw[16];
-          if (rrow) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const __half2* rh = reinterpret_cast<const __half2*>(&res[j]);
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                // The matmul result is an fp16 tensor in the unfused plan:
-                // round it, then add the residual in fp32 and round again.
-                const float2 fm = __half22float2(
-                    __floats2half2_rn(v[8 * j + 2 * q], v[8 * j + 2 * q + 1]));
-                const float2 fr = __half22float2(rh[q]);
-                hw[4 * j + q] = pack_half2(fr.x + fm.x, fr.y + fm.y);
-              }
-            }
-          } else {
-#pragma unroll
-            for (int q = 0; q < 16; ++q) hw[q] = pack_half2(v[2 * q], v[2 * q + 1]);
-          }
-#pragma unroll
-          for (int q = 0; q < 16; ++q) packed[h][q] = hw[q];
-        }
-        if (ROPE) {
-          const int n64 = nb * BN + g * 64;
-          if (n64 < p.rope_cols && row_ok) {
-            const int tok = (int)(row % p.rope_T);
-            rope_head64(packed[0], packed[1], p.rope_cos + (int64_t)tok * 64,
-                        p.rope_sin + (int64_t)tok * 64);
-          }
-        }
-        // 8 x 16 B into the 128-byte row rl of the stage, swizzled
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int chunk = (h * 4 + j) ^ (rl & 7);
-            *reinterpret_cast<uint4*>(stage + rl * 128 + chunk * 16) =
-                make_uint4(packed[h][4 * j], packed[h][4 * j + 1], packed[h][4 * j + 2],
-                           packed[h][4 * j + 3]);
-          }
-        fence_proxy_async_shared();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_3d(&tmC, stage, nb * BN + g * 64, mb * BM + quarter * 32, (int)b);
-          bulk_commit_group();
-        }
-      }
+      epilogue_tile<ROPE>(p, &tmC, tmem_base + (uint32_t)(acc * BN), stage, quarter, lane,
+                          g_lo, g_hi, b, (int64_t)mb * BM, nb * BN);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -366,6 +378,206 @@ done:
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+// ---- CTA-pair GEMM ---------------------------------------------------------
+//
+// The same persistent warp-specialised structure run by clusters of two CTAs
+// on two SMs that share one 256 x 256 output tile through tcgen05's pair mode
+// (cta_group::2). Per 64-deep k-block each CTA lands only its own 128 rows of
+// A and its own 128 columns of W (32 KiB), and the leader's single MMA thread
+// multiplies the whole 256 x 256 x 64 block across both SMs' tensor cores:
+// per SM that is the work of a 128 x 256 tile for two thirds of the shared-
+// memory fill traffic, which is what bounds the one-CTA kernel.
+//
+//   full[s]   leader only: both CTAs' TMA loads count their bytes on it;
+//             the leader's producer posts the expected 2 x 32 KiB.
+//   empty[s]  in both CTAs: the leader's MMA commit arrives on both when the
+//             stage's shared memory has been read.
+//   tfull[a]  in both CTAs: accumulator a of this CTA's rows is complete.
+//   tempty[a] leader only: all 16 epilogue warps of the pair have drained a.
+//
+// A wait that gives up raises the abort flag of both CTAs, so the pair
+// unwinds together and meets at the closing cluster barrier.
+struct PairCfg {
+  static constexpr int BN = 256;                     // columns of the pair's tile
+  static constexpr int STAGES = 6;
+  static constexpr int A_BYTES = BM * BK * 2;        // 16 KiB: this CTA's 128 rows
+  static constexpr int B_BYTES = (BN / 2) * BK * 2;  // 16 KiB: this CTA's 128 columns
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN;           // two fp32 accumulators
+  static constexpr int STAGING = kEpiWarps * 4096;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGING + 1024 + 256;
+};
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_f16_pair(const __grid_constant__ CUtensorMap tmA,
+                  const __grid_constant__ CUtensorMap tmB,
+                  const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
+  using Cfg = PairCfg;
+  constexpr int BN = Cfg::BN;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + Cfg::STAGES * Cfg::A_BYTES;
+  uint8_t* sOut = sB + Cfg::STAGES * Cfg::B_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + Cfg::STAGING);
+  uint64_t* empty = full + Cfg::STAGES;
+  uint64_t* tfull = empty + Cfg::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Cfg::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 2 * kEpiWarps);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();            // both CTAs' barriers initialised, TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t full_lead = cluster_addr(full, 0);
+  const uint32_t tempty_lead = cluster_addr(tempty, 0);
+  const uint32_t peer_abort = cluster_addr(tmem_slot + 1, rank ^ 1u);
+
+  const int64_t tiles_per_batch = (int64_t)p.tiles_m * p.tiles_n;
+  const int64_t pair_id = blockIdx.x >> 1;
+  const int64_t n_pairs = gridDim.x >> 1;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int64_t t = pair_id; t < p.total_tiles; t += n_pairs) {
+        const int64_t b = t / tiles_per_batch;
+        const int64_t r = t - b * tiles_per_batch;
+        const int mb = (int)(r / p.tiles_n);
+        const int nb = (int)(r % p.tiles_n);
+        const int bz = p.b_shared ? 0 : (int)b;
+        const int row = mb * (2 * BM) + (int)rank * BM;
+        const int col = nb * BN + (int)rank * (BN / 2);
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait_cluster(&empty[stage], phase ^ 1u, abort_flag, p.err)) {
+            st_cluster_u32(peer_abort, 1);
+            goto done;
+          }
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::STAGE_BYTES);
+          const uint32_t fb = full_lead + (uint32_t)(stage * 8);
+          tma_load_3d_pair(&tmA, fb, sA + stage * Cfg::A_BYTES, kb * BK, row, (int)b);
+#pragma unroll
+          for (int j = 0; j < BN / 128; ++j)
+            tma_load_3d_pair(&tmB, fb, sB + stage * Cfg::B_BYTES + j * (BK * 128),
+                             col + j * 64, kb * BK, bz);
+          if (++stage == Cfg::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = idesc_f16_f32(2 * BM, BN, false, true);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int64_t t = pair_id; t < p.total_tiles; t += n_pairs) {
+        if (!mbar_wait_cluster(&tempty[acc], acc_phase ^ 1u, abort_flag, p.err)) {
+          st_cluster_u32(peer_abort, 1);
+          goto done;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait_cluster(&full[stage], phase, abort_flag, p.err)) {
+            st_cluster_u32(peer_abort, 1);
+            goto done;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * Cfg::A_BYTES);
+          const uint32_t b0 = smem_u32(sB + stage * Cfg::B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = sdesc_sw128(a0 + kk * 32, 16, 1024);
+            const uint64_t bd = sdesc_sw128(b0 + kk * 2048, BK * 128, 1024);
+            umma_f16_pair(d_tmem, ad, bd, idesc, (kb | kk) ? 1u : 0u);
+          }
+          umma_commit_pair(&empty[stage], 0x3);
+          if (++stage == Cfg::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        umma_commit_pair(&tfull[acc], 0x3);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+    }
+  } else {
+    const int ew = warp - 2;
+    const int quarter = warp & 3;
+    const int colhalf = ew >> 2;
+    constexpr int kGroups = BN / 64;
+    const int g_lo = colhalf * (kGroups / 2);
+    const int g_hi = (colhalf + 1) * (kGroups / 2);
+    uint8_t* stage = sOut + ew * 4096;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int64_t t = pair_id; t < p.total_tiles; t += n_pairs) {
+      const int64_t b = t / tiles_per_batch;
+      const int64_t r = t - b * tiles_per_batch;
+      const int mb = (int)(r / p.tiles_n);
+      const int nb = (int)(r % p.tiles_n);
+      const bool ok = mbar_wait_cluster(&tfull[acc], acc_phase, abort_flag, p.err);
+      if (!__all_sync(0xffffffffu, ok)) {
+        if (lane == 0) st_cluster_u32(peer_abort, 1);
+        goto done;
+      }
+      tc_fence_after();
+      epilogue_tile<false>(p, &tmC, tmem_base + (uint32_t)(acc * BN), stage, quarter, lane,
+                           g_lo, g_hi, b, (int64_t)mb * (2 * BM) + rank * BM, nb * BN);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_lead + (uint32_t)(acc * 8));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+  }
+
+done:
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();            // no CTA leaves while the other may still use it
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
   }
 }
 
@@ -492,6 +704,62 @@ bool aligned16(const void* p) {
   return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
 }
 
+// Pairs that fit on the device at once (0: the pair kernel is not used),
+// found once by the occupancy calculator for clusters of two.
+int g_pair_clusters = 0;
+
+int launch_pair(const GemmDesc& g, int* err, cudaStream_t s) {
+  using Cfg = PairCfg;
+  CUtensorMap ta, tb, tcm;
+  // A: dims (K, M, batch); box (64, 128, 1) -- one CTA's rows.
+  if (!make_tmap_3d_f16(&ta, g.A, (uint64_t)g.K, (uint64_t)g.M, (uint64_t)g.batch, BK, BM))
+    return -1;
+  // W: dims (N, K, batch or 1); box (64, 64, 1); two per CTA per stage.
+  if (!make_tmap_3d_f16(&tb, g.B, (uint64_t)g.N, (uint64_t)g.K,
+                        (uint64_t)(g.b_shared ? 1 : g.batch), 64, BK))
+    return -1;
+  if (!make_tmap_3d_f16(&tcm, g.out, (uint64_t)g.N, (uint64_t)g.M, (uint64_t)g.batch, 64, 32))
+    return -1;
+  GemmParams p;
+  p.M = g.M;
+  p.K = g.K;
+  p.N = g.N;
+  p.batch = g.batch;
+  p.tiles_m = (int)((g.M + 2 * BM - 1) / (2 * BM));   // 256-row pair tiles
+  p.tiles_n = (g.N + Cfg::BN - 1) / Cfg::BN;
+  p.total_tiles = g.batch * (int64_t)p.tiles_m * p.tiles_n;
+  p.num_kb = (g.K + BK - 1) / BK;
+  p.b_shared = g.b_shared ? 1 : 0;
+  p.act = g.act;
+  p.bias = g.bias;
+  p.resid = reinterpret_cast<const __half*>(g.resid);
+  p.out = reinterpret_cast<__half*>(g.out);
+  p.err = err;
+  p.rope_cos = nullptr;
+  p.rope_sin = nullptr;
+  p.rope_T = 1;
+  p.rope_cols = 0;
+  const int64_t pairs =
+      p.total_tiles < g_pair_clusters ? p.total_tiles : (int64_t)g_pair_clusters;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
+  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, gemm_f16_pair, ta, tb, tcm, p) != cudaSuccess) {
+    cudaGetLastError();
+    return HEXLIB_B200_ERR_CUDA;
+  }
+  return HEXLIB_B200_OK;
+}
+
 }  // namespace
 
 int gemm_kernels_init() {
@@ -516,6 +784,28 @@ int gemm_kernels_init() {
   cudaFuncAttributes fa;
   cudaError_t e7 = cudaFuncGetAttributes(&fa, gemm_f16_simt);
   sm_count();
+  // The pair kernel: HEXLIB_B200_GEMM_PAIR=0 turns it off (for comparisons).
+  g_pair_clusters = 0;
+  const char* env = getenv("HEXLIB_B200_GEMM_PAIR");
+  if (!(env && env[0] == '0') &&
+      cudaFuncSetAttribute(gemm_f16_pair, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           PairCfg::SMEM_BYTES) == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (unsigned)sm_count(), 1, 1);
+    cfg.blockDim = dim3(kGemmThreads, 1, 1);
+    cfg.dynamicSmemBytes = PairCfg::SMEM_BYTES;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_f16_pair, &cfg) == cudaSuccess && n > 0)
+      g_pair_clusters = n;
+    cudaGetLastError();
+  }
   if (e1 != cudaSuccess || e2 != cudaSuccess || e3 != cudaSuccess || e4 != cudaSuccess ||
       e5 != cudaSuccess || e6 != cudaSuccess || e7 != cudaSuccess) {
     cudaGetLastError();
@@ -540,7 +830,9 @@ int launch_gemm(const GemmDesc& g, int* err, cudaStream_t s) {
                       (!g.resid || aligned16(g.resid)) && tma_available();
   if (tma_ok) {
     int rc;
-    if (g.N % 256 == 0)
+    if (g.N % 256 == 0 && !rope && g_pair_clusters > 0)
+      rc = launch_pair(g, err, s);
+    else if (g.N % 256 == 0)
       rc = rope ? launch_tc<256, true>(g, err, s) : launch_tc<256, false>(g, err, s);
     else if (g.N % 128 == 0)
       rc = rope ? launch_tc<128, true>(g, err, s) : launch_tc<128, false>(g, err, s);

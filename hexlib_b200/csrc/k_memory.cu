@@ -38,6 +38,9 @@ bool aligned16(const void* p) {
   return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
 }
 
+// CTAs of layernorm_f16_reg<VPL> resident on the whole device (index VPL).
+int g_ln_resident[5] = {0, 0, 0, 0, 0};
+
 union H8 {
   uint4 u;
   __half2 h2[4];
@@ -204,19 +207,31 @@ __global__ void layernorm_f16_reg(const uint4* __restrict__ x,
   const int lane = threadIdx.x & 31;
   const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  // Software pipelined: the loads of the warp's next row are in flight while
+  // this row is reduced and written, so each warp keeps two rows of HBM
+  // reads outstanding instead of one.
+  uint4 nxt[VPL];
+  if (warp0 < R) {
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) nxt[j] = __ldg(x + warp0 * (C / 8) + j * 32 + lane);
+  }
   for (int64_t r = warp0; r < R; r += nwarps) {
-    const uint4* xr = x + r * (C / 8);
     float v[VPL][8];
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
       H8 h;
-      h.u = __ldg(xr + j * 32 + lane);
+      h.u = nxt[j];
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         float2 f = __half22float2(h.h2[q]);
         v[j][2 * q] = f.x;
         v[j][2 * q + 1] = f.y;
       }
+    }
+    if (r + nwarps < R) {
+#pragma unroll
+      for (int j = 0; j < VPL; ++j)
+        nxt[j] = __ldg(x + (r + nwarps) * (C / 8) + j * 32 + lane);
     }
     float s = 0.f;
 #pragma unroll
@@ -747,6 +762,21 @@ int memory_kernels_init() {
     }
   }
   grid_for(1, kThreads);
+  const void* ln[5] = {nullptr, (const void*)layernorm_f16_reg<1>,
+                       (const void*)layernorm_f16_reg<2>, (const void*)layernorm_f16_reg<3>,
+                       (const void*)layernorm_f16_reg<4>};
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  for (int v = 1; v <= 4; ++v) {
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, ln[v], kThreads, 0) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      per_sm = 0;
+    }
+    g_ln_resident[v] = per_sm * sms;
+  }
   return HEXLIB_B200_OK;
 }
 
@@ -841,7 +871,12 @@ int launch_layernorm_f16(const void* x, const float* w, const float* b,
   if (R < 0 || C <= 0) return HEXLIB_B200_ERR_INVAL_PARAMS;
   if (R == 0) return HEXLIB_B200_OK;
   const bool al = aligned16(x) && aligned16(y) && aligned16(w) && aligned16(b);
-  const int grid = grid_for(R * 32, kThreads);
+  int grid = grid_for(R * 32, kThreads);
+  // The register kernels loop over rows: launch only as many CTAs as stay
+  // resident, so every warp keeps its two rows of loads in flight.
+  const int vpl = (C % 256 == 0 && C <= 1024) ? C / 256 : 0;
+  if (al && vpl > 0 && g_ln_resident[vpl] > 0 && grid > g_ln_resident[vpl])
+    grid = g_ln_resident[vpl];
   if (al && C == 256)
     layernorm_f16_reg<1><<<grid, kThreads, 0, s>>>(
         (const uint4*)x, w, b, (uint4*)y, R, eps);

@@ -117,6 +117,18 @@ class Session:
         p, n = _host_ptr(host)
         _ok(f"buf_read fd {fd}", self._L.hexlib_b200_buf_read(self._h, fd, offset, p, n))
 
+    def write_async(self, fd: int, offset: int, host) -> None:
+        """Enqueue the copy on the session stream; `host` must stay valid until
+        sync() and be page-locked for the copy to overlap other streams."""
+        p, n = _host_ptr(host)
+        _ok(f"buf_write_async fd {fd}",
+            self._L.hexlib_b200_buf_write_async(self._h, fd, offset, p, n))
+
+    def read_async(self, fd: int, offset: int, host) -> None:
+        p, n = _host_ptr(host)
+        _ok(f"buf_read_async fd {fd}",
+            self._L.hexlib_b200_buf_read_async(self._h, fd, offset, p, n))
+
     def device_ptr(self, fd: int) -> tuple[int, int]:
         p, n = ctypes.c_uint64(), ctypes.c_uint64()
         _ok("buf_device_ptr", self._L.hexlib_b200_buf_device_ptr(self._h, fd, ctypes.byref(p),
@@ -151,20 +163,23 @@ class Session:
             raise ValueError(f"{name!r} is a const")
         return p.offset * n_images, p.nbytes * n_images
 
-    def write_input(self, name: str, host, n_images: int) -> None:
+    def write_input(self, name: str, host, n_images: int, wait: bool = True) -> None:
         off, nb = self.tensor_offset(name, n_images)
         _, have = _host_ptr(host)
         if have != nb:
             raise ValueError(f"input {name!r} for {n_images} images is {nb} bytes, got {have}")
-        self.write(IMAGE_FD, off, host)
+        (self.write if wait else self.write_async)(IMAGE_FD, off, host)
 
-    def read_output(self, name: str, n_images: int, out=None) -> np.ndarray:
+    def read_output(self, name: str, n_images: int, out=None, wait: bool = True) -> np.ndarray:
         p = self._need().placements[name]
         off, nb = self.tensor_offset(name, n_images)
         if out is None:
             out = np.empty((n_images,) + tuple(p.shape),
                            {"fp16": np.float16, "fp32": np.float32}[p.dtype])
-        self.read(IMAGE_FD, off, out)
+        _, have = _host_ptr(out)
+        if have != nb:
+            raise ValueError(f"output {name!r} for {n_images} images is {nb} bytes, got {have}")
+        (self.read if wait else self.read_async)(IMAGE_FD, off, out)
         return out
 
     def invoke(self, n_images: int, mode: int = MODE_GRAPH, sync: bool = True) -> wire.BatchResponse:
@@ -214,6 +229,69 @@ class Session:
                 "strides": None,
             }
         return torch.as_tensor(_View(), device=f"cuda:{self.device}")
+
+
+class Pipeline:
+    """Back-to-back batches of one plan through `depth` sessions on one device,
+    used in turn. A step's upload, graph replay and read-back are enqueued on
+    its session's stream without waiting, so the copy engines move the next
+    step's images (and the previous step's embeddings) while the SMs run this
+    one; each session's stream keeps its own steps in order.
+
+        pipe = Pipeline(plan, max_images=64)
+        for k, batch in enumerate(batches):          # page-locked host arrays
+            pipe.submit(batch, outs[k])
+        pipe.drain()                                 # every outs[k] is filled
+
+    A host array handed to submit() must stay untouched until the step is
+    retired: by drain(), or by the submit() that reuses its session
+    (`depth` submits later), which waits for it first. Device-side failures
+    raise B200Error at that wait.
+    """
+
+    def __init__(self, plan: CudaPlan, max_images: int, device: int = 0, depth: int = 2,
+                 sessions: list[Session] | None = None) -> None:
+        if len(plan.inputs) != 1 or len(plan.outputs) != 1:
+            raise ValueError("Pipeline serves single-input single-output plans")
+        if depth < 1:
+            raise ValueError("depth must be >= 1")
+        self.plan = plan
+        self.sessions = list(sessions or [])
+        self._own = len(self.sessions)
+        for s in self.sessions:
+            if s.plan is not plan or s.max_images < max_images:
+                raise ValueError("a shared session must hold this plan for max_images")
+        while len(self.sessions) < depth:
+            s = Session(device)
+            s.load(plan, max_images)
+            self.sessions.append(s)
+        self._busy = [False] * len(self.sessions)
+        self._next = 0
+
+    def submit(self, images, out) -> Session:
+        """Enqueue one batch; returns the session whose stream carries it."""
+        k = self._next
+        s = self.sessions[k]
+        if self._busy[k]:
+            s.sync()
+        n = int(images.shape[0])
+        s.write_input(self.plan.inputs[0], images, n, wait=False)
+        self._busy[k] = True
+        s.invoke(n, sync=False)
+        s.read_output(self.plan.outputs[0], n, out, wait=False)
+        self._next = (k + 1) % len(self.sessions)
+        return s
+
+    def drain(self) -> None:
+        for k, s in enumerate(self.sessions):
+            if self._busy[k]:
+                self._busy[k] = False
+                s.sync()
+
+    def close(self) -> None:
+        """Close the sessions this pipeline opened (not ones it was handed)."""
+        for s in self.sessions[self._own:]:
+            s.close()
 
 
 def attention_available() -> bool:

@@ -139,6 +139,17 @@ HEXLIB_B200_API int hexlib_b200_buf_write(hexlib_b200_ctx *ctx, uint32_t fd, uin
                           const void *src, uint64_t nbytes);
 HEXLIB_B200_API int hexlib_b200_buf_read(hexlib_b200_ctx *ctx, uint32_t fd, uint64_t offset,
                          void *dst, uint64_t nbytes);
+/* The same copies, returning once they are enqueued on the session stream
+ * (no reference counterpart: the reference's buffers are host-mapped memory
+ * the DSP reads in place, so its writes need no copy at all). Ordered with
+ * the session's invokes; `src`/`dst` must stay valid and unmodified until a
+ * later hexlib_b200_sync() returns, and must be page-locked (cudaHostAlloc /
+ * cudaHostRegister) for the copy to overlap kernels of another stream. */
+HEXLIB_B200_API int hexlib_b200_buf_write_async(hexlib_b200_ctx *ctx, uint32_t fd,
+                                                uint64_t offset, const void *src,
+                                                uint64_t nbytes);
+HEXLIB_B200_API int hexlib_b200_buf_read_async(hexlib_b200_ctx *ctx, uint32_t fd,
+                                               uint64_t offset, void *dst, uint64_t nbytes);
 /* The device address of a buffer, for callers that hand it to NCCL/torch. */
 HEXLIB_B200_API int hexlib_b200_buf_device_ptr(hexlib_b200_ctx *ctx, uint32_t fd,
                                uint64_t *ptr, uint64_t *alloc_bytes);

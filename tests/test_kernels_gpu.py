@@ -216,6 +216,10 @@ ACT = {"none": 0, "gelu_tanh": 1, "gelu_erf": 2}
     (256, 1536, 768, "none"),
     (200, 128, 200, "gelu_tanh"),   # M and N tails on the tensor-core path
     (1000, 64, 64, "none"),
+    # N % 256 == 0 runs on CTA pairs (256-row tiles split over two SMs):
+    (300, 768, 512, "none"),        # the second CTA's rows end inside its tile
+    (128, 200, 256, "gelu_tanh"),   # the second CTA's rows are all past M; K tail
+    (8192, 512, 2304, "none"),      # several tiles per pair, accumulators cycle
     (20, 40, 96, "gelu_erf"),       # K % 8 != 0 -> CUDA-core fallback
     (3, 64, 30, "none"),            # N % 8 != 0 -> fallback
 ])
@@ -266,6 +270,7 @@ def test_matmul_epilogue_residual():
     (3, 40, 128, 200),     # the matmul harness shape
     (2, 1024, 64, 1024),   # QK^T at 512^2, two heads
     (4, 64, 16, 64),       # tiny head dim
+    (3, 200, 64, 512),     # pair tiles with an M tail inside each batch entry
 ])
 def test_matmul_batched(Bn, M, K, N):
     a = randn16((Bn, M, K), 31)

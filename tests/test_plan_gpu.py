@@ -132,6 +132,32 @@ def test_graph_replay_and_eager_mode_agree_bit_for_bit(enc256):
     assert [r.kind for r in r3.results] == [r.kind for r in r1.results]
 
 
+def test_pipelined_batches_equal_one_at_a_time_runs(enc256):
+    """Five different batches through a depth-2 pipeline (uploads and read-
+    backs overlapping the other session's replay, page-locked host arrays)
+    give each batch the bits a plain Session.run gives it."""
+    import torch
+    from hexlib_b200.session import Pipeline
+    cfg, g, w, imgs, refs = enc256
+    plan = wholeplan.build_cuda_plan(G.compile_for_cuda(g, residual=True), w, alias=True)
+    batches = [np.ascontiguousarray(np.roll(imgs[:2], k, axis=-1)) for k in range(5)]
+    shape = (2,) + tuple(plan.placements[plan.outputs[0]].shape)
+    pin_in = [torch.from_numpy(b).pin_memory() for b in batches]
+    pin_out = [torch.empty(shape, dtype=torch.float16).pin_memory() for _ in batches]
+    with Session(0) as s:
+        s.load(plan, max_images=2)
+        want = [s.run(b) for b in batches]
+        pipe = Pipeline(plan, max_images=2, sessions=[s])
+        try:
+            for b, o in zip(pin_in, pin_out):
+                pipe.submit(b, o)
+            pipe.drain()
+        finally:
+            pipe.close()
+    for k in range(5):
+        np.testing.assert_array_equal(pin_out[k].numpy(), want[k], err_msg=f"batch {k}")
+
+
 def _patch_op_kind(blob: bytes, i: int, kind: int) -> bytes:
     b = bytearray(blob)
     off = wire.HDR.unpack_from(blob)[8] + i * wire.OP_SIZE
