@@ -67,6 +67,13 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// max(a, b, c) in one instruction (sm_100's three-input form).
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -230,61 +237,68 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         for (int i = 0; i < AT_BN; ++i)
           if (i >= valid) sv[i] = __float_as_uint(-INFINITY);
       }
-      float pm[8];
+      // row max: four chains of three-input maxima
+      float pm[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) pm[i] = __uint_as_float(sv[i]);
+      for (int i = 0; i < 4; ++i) pm[i] = __uint_as_float(sv[i]);
 #pragma unroll
-      for (int i = 8; i < AT_BN; ++i) pm[i & 7] = fmaxf(pm[i & 7], __uint_as_float(sv[i]));
+      for (int i = 4; i < AT_BN; i += 8)
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          pm[q] = max3f(pm[q], __uint_as_float(sv[i + q]), __uint_as_float(sv[i + 4 + q]));
       // the scale is positive, so max(s)*c is the max of s*c
-      const float mx = c * fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
-                                 fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
+      const float mx = c * max3f(pm[0], pm[1], fmaxf(pm[2], pm[3]));
       const bool rescale = mx > m_run + kRescale;
       const float m_use = rescale ? mx : m_run;
       const float alpha = rescale ? ex2_approx(m_run - mx) : 1.0f;
-      // p = 2^(s*c - m), eight partial row sums, packed to fp16
-      float ps[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) ps[i] = 0.f;
-      uint32_t h2[AT_BN / 2];
-#pragma unroll
-      for (int i = 0; i < AT_BN / 2; ++i) {
-        const float p0 = ex2_approx(fmaf(__uint_as_float(sv[2 * i]), c, -m_use));
-        const float p1 = ex2_approx(fmaf(__uint_as_float(sv[2 * i + 1]), c, -m_use));
-        ps[i & 7] += p0 + p1;
-        h2[i] = pack_half2(p0, p1);
-      }
-      const float rs = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
       // P V of the previous block must be done: it reads the P buffer this
-      // block overwrites, and a rescale must see its contribution in O.
+      // block overwrites, and a rescale (below) must see its contribution in O.
       if (j > 0) {
         const bool ok2 = mbar_wait(&o_full[t], (uint32_t)(j - 1) & 1u, abort_flag, p.err);
         if (!__all_sync(0xffffffffu, ok2)) goto done;
         tc_fence_after();
-        if (__any_sync(0xffffffffu, rescale)) {
+      }
+      // p = 2^(s*c - m), 32 keys at a time: one FMA and one MUFU exponential
+      // per key, eight partial row sums, and the fp16 pairs straight into this
+      // row of the 128B-swizzled P tile (keys [64a, 64a + 64) form one atom row).
+      float ps[8];
 #pragma unroll
-          for (int h = 0; h < AT_D / 32; ++h) {
-            uint32_t rg[32];
-            tmem_ld_32x32b_x32(o_col + h * 32, rg);
-            tmem_ld_wait();
+      for (int i = 0; i < 8; ++i) ps[i] = 0.f;
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-              rg[i] = __float_as_uint(__uint_as_float(rg[i]) * alpha);
-            tmem_st_32x32b_x32(o_col + h * 32, rg);
-          }
-          tmem_st_wait();
+      for (int k32 = 0; k32 < AT_BN / 32; ++k32) {
+        uint32_t h2[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int e = k32 * 32 + 2 * i;
+          const float p0 = ex2_approx(fmaf(__uint_as_float(sv[e]), c, -m_use));
+          const float p1 = ex2_approx(fmaf(__uint_as_float(sv[e + 1]), c, -m_use));
+          ps[(2 * i) & 7] += p0;
+          ps[(2 * i + 1) & 7] += p1;
+          h2[i] = pack_half2(p0, p1);
+        }
+        uint8_t* atom = prow + (k32 >> 1) * (AT_BM * 128);
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const int chunk = ((k32 & 1) * 4 + g) ^ (r & 7);
+          *reinterpret_cast<uint4*>(atom + chunk * 16) =
+              make_uint4(h2[4 * g], h2[4 * g + 1], h2[4 * g + 2], h2[4 * g + 3]);
         }
       }
-      // P to shared memory: keys [64a, 64a + 64) form one 128-byte atom row
+      const float rs = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+      // O *= alpha before P V of this block is issued (rare: the max grew by
+      // more than 2^8 since the last rescale)
+      if (j > 0 && __any_sync(0xffffffffu, rescale)) {
 #pragma unroll
-      for (int a = 0; a < 2; ++a) {
-        uint8_t* atom = prow + a * (AT_BM * 128);
+        for (int h = 0; h < AT_D / 32; ++h) {
+          uint32_t rg[32];
+          tmem_ld_32x32b_x32(o_col + h * 32, rg);
+          tmem_ld_wait();
 #pragma unroll
-        for (int g = 0; g < 8; ++g) {
-          const int chunk = g ^ (r & 7);
-          const int q = a * 32 + 4 * g;
-          *reinterpret_cast<uint4*>(atom + chunk * 16) =
-              make_uint4(h2[q], h2[q + 1], h2[q + 2], h2[q + 3]);
+          for (int i = 0; i < 32; ++i)
+            rg[i] = __float_as_uint(__uint_as_float(rg[i]) * alpha);
+          tmem_st_32x32b_x32(o_col + h * 32, rg);
         }
+        tmem_st_wait();
       }
       tc_fence_before();
       fence_proxy_async_smem();
