@@ -53,6 +53,9 @@ def parse():
     ap.add_argument("--no-attention-fusion", action="store_true")
     ap.add_argument("--no-residual-fusion", action="store_true")
     ap.add_argument("--no-qkv-fusion", action="store_true")
+    ap.add_argument("--sweep", action="store_true",
+                    help="instead of the encoder: the memory-bound kernel sweep (one GPU), "
+                         "one JSON line per kernel and shape")
     return ap.parse_args()
 
 
@@ -447,9 +450,29 @@ def run_b200(args) -> None:
         pg.destroy_process_group()
 
 
+def run_sweep(args) -> None:
+    """The memory-bound kernel sweep (hexlib_b200/sweep.py) on this rank's GPU;
+    rank 0 prints, other ranks exit."""
+    import torch
+
+    from hexlib_b200 import dist as D
+    from hexlib_b200 import sweep
+    rank, local, _ = D.env_rank()
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    pk = peaks()
+    for row in sweep.run(pk["hbm"]):
+        row["peak_gbs"] = pk["hbm"]
+        row["peak_source"] = f"{pk['src']} (hbm copy)"
+        print(json.dumps(row), flush=True)
+
+
 def main():
     args = parse()
-    if args.impl == "reference":
+    if args.sweep:
+        run_sweep(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_b200(args)

@@ -257,6 +257,19 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc,
       : "memory");
 }
 
+// The same with A read from tensor memory: `a_tmem` addresses lane 0 of an
+// M x 16 K-slice whose row i sits in lane i, two fp16 per 32-bit column.
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem,
+                                            uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accum)
+      : "memory");
+}
+
 // Arrive once on `bar` when every tcgen05.mma this thread issued so far has
 // completed (and, with it, its shared-memory reads).
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {

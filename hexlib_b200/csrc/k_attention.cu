@@ -9,12 +9,14 @@
 // 128-row tiles (a and b) and streams the keys in blocks of 128:
 //   warp 0     TMA: both Q tiles once, then K and V blocks into a 3-stage ring;
 //   warp 1     one lane issues tcgen05.mma: S_t = Q_t K^T (M=128, N=128,
-//              K=64) into TMEM, and after the softmax has written P_t to shared
-//              memory, O_t = P_t V (M=128, N=64, K=128) into TMEM;
+//              K=64) into TMEM, and after the softmax has written P_t to
+//              TMEM, O_t = P_t V (M=128, N=64, K=128) with A read from TMEM;
 //   warps 2-5  softmax of tile a, warps 6-9 softmax of tile b: one query row
 //              per thread, the block's scores read from TMEM in one pass,
-//              P written to shared memory; the output accumulates in TMEM and
-//              is rescaled there only when the running max grows by > 2^8.
+//              P (fp16) written back to TMEM; the output accumulates in TMEM
+//              and is rescaled there only when the running max grows by > 2^8.
+// TMEM columns: S_a [0,128), S_b [128,256), O_a [256,320), O_b [320,384),
+// P_a [384,448), P_b [448,512).
 // While one tile's softmax runs, the tensor core works on the other tile's
 // products, so the exp units and the tensor core overlap.
 //
@@ -43,9 +45,8 @@ constexpr int AT_D = 64;
 constexpr int AT_STAGES = 3;
 constexpr int AT_THREADS = 320;
 constexpr int AT_TILE = AT_BM * AT_D * 2;        // 16 KiB: one Q, K or V tile
-constexpr int AT_P = AT_BM * AT_BN * 2;          // 32 KiB: P as two 64-key atoms
-constexpr int AT_SMEM = 2 * AT_TILE + AT_STAGES * 2 * AT_TILE + 2 * AT_P + 1024 + 256;
-constexpr uint32_t AT_TMEM_COLS = 512;           // S_a, S_b: 128 each; O_a, O_b: 64 each
+constexpr int AT_SMEM = 2 * AT_TILE + AT_STAGES * 2 * AT_TILE + 1024 + 256;
+constexpr uint32_t AT_TMEM_COLS = 512;           // S_a, S_b: 128; O_a, O_b, P_a, P_b: 64
 
 struct AttnParams {
   int T;
@@ -74,10 +75,6 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
   return d;
 }
 
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
 __global__ void __launch_bounds__(AT_THREADS, 1)
     attention_tc(const __grid_constant__ CUtensorMap tmQ,
                  const __grid_constant__ CUtensorMap tmK,
@@ -88,8 +85,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   uint8_t* sQ = smem;                                  // [2][16 KiB]
   uint8_t* sK = sQ + 2 * AT_TILE;                      // [STAGES][16 KiB]
   uint8_t* sV = sK + AT_STAGES * AT_TILE;              // [STAGES][16 KiB]
-  uint8_t* sP = sV + AT_STAGES * AT_TILE;              // [2][32 KiB]
-  uint64_t* q_full = reinterpret_cast<uint64_t*>(sP + 2 * AT_P);
+  uint64_t* q_full = reinterpret_cast<uint64_t*>(sV + AT_STAGES * AT_TILE);
   uint64_t* kv_full = q_full + 1;
   uint64_t* kv_empty = kv_full + AT_STAGES;
   uint64_t* s_full = kv_empty + AT_STAGES;   // [2]
@@ -177,14 +173,13 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         const int st = j % AT_STAGES;
         if (!mbar_wait(&p_full[t], (uint32_t)j & 1u, abort_flag, p.err)) return false;
         tc_fence_after();
-        const uint32_t pa = smem_u32(sP + t * AT_P);
+        const uint32_t pa = tmem + 384u + (uint32_t)(t * 64);   // 16 keys = 8 columns
         const uint32_t vb = smem_u32(sV + st * AT_TILE);
 #pragma unroll
         for (int kk = 0; kk < AT_BN / 16; ++kk)
-          umma_f16(tmem + 256u + (uint32_t)(t * AT_D),
-                   sdesc_sw128(pa + (kk >> 2) * (AT_BM * 128) + (kk & 3) * 32, 16, 1024),
-                   sdesc_sw128(vb + kk * 2048, 8192, 1024), idesc_o,
-                   (j > 0 || kk > 0) ? 1u : 0u);
+          umma_f16_ts(tmem + 256u + (uint32_t)(t * AT_D), pa + (uint32_t)(kk * 8),
+                      sdesc_sw128(vb + kk * 2048, 8192, 1024), idesc_o,
+                      (j > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&o_full[t]);
         return true;
       };
@@ -212,7 +207,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t s_col = tmem + lane_off + (uint32_t)(t * AT_BN);
     const uint32_t o_col = tmem + lane_off + 256u + (uint32_t)(t * AT_D);
-    uint8_t* prow = sP + t * AT_P + r * 128;
+    const uint32_t p_col = tmem + lane_off + 384u + (uint32_t)(t * 64);
     const float c = p.c_log2;
     constexpr float kRescale = 8.0f;
     float m_run = -INFINITY, l_run = 0.f;
@@ -259,8 +254,8 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         tc_fence_after();
       }
       // p = 2^(s*c - m), 32 keys at a time: one FMA and one MUFU exponential
-      // per key, eight partial row sums, and the fp16 pairs straight into this
-      // row of the 128B-swizzled P tile (keys [64a, 64a + 64) form one atom row).
+      // per key, eight partial row sums, and the fp16 pairs stored to this
+      // row's lane of P in TMEM (column i holds keys 2i and 2i + 1).
       float ps[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) ps[i] = 0.f;
@@ -276,13 +271,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
           ps[(2 * i + 1) & 7] += p1;
           h2[i] = pack_half2(p0, p1);
         }
-        uint8_t* atom = prow + (k32 >> 1) * (AT_BM * 128);
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          const int chunk = ((k32 & 1) * 4 + g) ^ (r & 7);
-          *reinterpret_cast<uint4*>(atom + chunk * 16) =
-              make_uint4(h2[4 * g], h2[4 * g + 1], h2[4 * g + 2], h2[4 * g + 3]);
-        }
+        tmem_st_32x32b_x16(p_col + (uint32_t)(k32 * 16), h2);
       }
       const float rs = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
       // O *= alpha before P V of this block is issued (rare: the max grew by
@@ -300,8 +289,8 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         }
         tmem_st_wait();
       }
+      tmem_st_wait();                  // P (and a rescaled O) are in TMEM
       tc_fence_before();
-      fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[t]);
       l_run = l_run * alpha + rs;

@@ -12,6 +12,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <unordered_map>
+
 #include "hb_kernels.h"
 
 namespace hb {
@@ -38,8 +40,9 @@ bool aligned16(const void* p) {
   return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
 }
 
-// CTAs of layernorm_f16_reg<VPL> resident on the whole device (index VPL).
-int g_ln_resident[5] = {0, 0, 0, 0, 0};
+// CTAs of each row kernel that stay resident on the whole device, filled
+// once by memory_kernels_init (read-only afterwards).
+std::unordered_map<const void*, int> g_resident;
 
 union H8 {
   uint4 u;
@@ -193,84 +196,237 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-// ---- layernorm ----------------------------------------------------------------
-// One warp per row, the row held in registers as VPL 16-byte vectors per lane
-// (C = 256 * VPL). Two passes over the registers: the mean, then the biased
-// variance of the centred values (kernels/layernorm_fp16/kernel_api.h:7-29).
+// ---- row kernels: layernorm, rmsnorm, softmax --------------------------------------
+// ROW LAYOUT. A row of C = G * V * 8 fp16 is owned by G threads and held in
+// their registers as V 16-byte vectors each: vector j*G + g of the row is
+// thread g's j-th, so the G threads read G consecutive vectors per access.
+// G = 8, 16 or 32 are lanes of one warp (32 / G rows per warp, shuffles of
+// width G); G = 256 is a whole CTA (one row per CTA, a shared-memory combine
+// across its 8 warps) for rows of 2048 and more. Each warp or CTA walks its
+// rows with the next row's loads in flight while the current one is reduced,
+// and the launcher sizes the grid to the CTAs that stay resident.
 
-template <int VPL>
-__global__ void layernorm_f16_reg(const uint4* __restrict__ x,
-                                  const float* __restrict__ w,
-                                  const float* __restrict__ b,
-                                  uint4* __restrict__ y, int64_t R, float eps) {
-  constexpr int C = VPL * 256;
-  const int lane = threadIdx.x & 31;
-  const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
-  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  // Software pipelined: the loads of the warp's next row are in flight while
-  // this row is reduced and written, so each warp keeps two rows of HBM
-  // reads outstanding instead of one.
-  uint4 nxt[VPL];
-  if (warp0 < R) {
+template <int G>
+__device__ __forceinline__ float row_sum(float v, float* red) {
+  if constexpr (G <= 32) {
 #pragma unroll
-    for (int j = 0; j < VPL; ++j) nxt[j] = __ldg(x + warp0 * (C / 8) + j * 32 + lane);
+    for (int o = G / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+  } else {
+    v = warp_sum(v);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < G / 32; ++i) t += red[i];
+    __syncthreads();  // red is reused by the next reduction
+    return t;
   }
-  for (int64_t r = warp0; r < R; r += nwarps) {
-    float v[VPL][8];
+}
+
+template <int G>
+__device__ __forceinline__ float row_max(float v, float* red) {
+  if constexpr (G <= 32) {
 #pragma unroll
-    for (int j = 0; j < VPL; ++j) {
-      H8 h;
-      h.u = nxt[j];
+    for (int o = G / 2; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+  } else {
+    v = warp_max(v);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float t = -INFINITY;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        float2 f = __half22float2(h.h2[q]);
-        v[j][2 * q] = f.x;
-        v[j][2 * q + 1] = f.y;
-      }
+    for (int i = 0; i < G / 32; ++i) t = fmaxf(t, red[i]);
+    __syncthreads();
+    return t;
+  }
+}
+
+// Which rows a thread walks: rows base + sub for base = first, first + step,
+// ... while base < R (uniform across the warp or CTA that shares a row), and
+// its index g within the row's G threads.
+template <int G>
+struct RowWalk {
+  int g, sub;
+  int64_t first, step;
+  __device__ RowWalk() {
+    if constexpr (G <= 32) {
+      const int lane = threadIdx.x & 31;
+      g = lane % G;
+      sub = lane / G;
+      const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+      first = warp * (32 / G);
+      step = (((int64_t)gridDim.x * blockDim.x) >> 5) * (32 / G);
+    } else {
+      g = threadIdx.x;
+      sub = 0;
+      first = blockIdx.x;
+      step = gridDim.x;
     }
-    if (r + nwarps < R) {
+  }
+};
+
+template <int G, int V>
+__device__ __forceinline__ void row_load(uint4 (&d)[V], const uint4* __restrict__ x,
+                                         int64_t r, int g) {
+  constexpr int C8 = G * V;
 #pragma unroll
-      for (int j = 0; j < VPL; ++j)
-        nxt[j] = __ldg(x + (r + nwarps) * (C / 8) + j * 32 + lane);
+  for (int j = 0; j < V; ++j) d[j] = __ldg(x + r * C8 + j * G + g);
+}
+
+template <int V>
+__device__ __forceinline__ void unpack_rows(float (&v)[V][8], const uint4 (&d)[V]) {
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    H8 h;
+    h.u = d[j];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 f = __half22float2(h.h2[q]);
+      v[j][2 * q] = f.x;
+      v[j][2 * q + 1] = f.y;
     }
+  }
+}
+
+// layernorm: the mean, then the biased variance of the centred values
+// (kernels/layernorm_fp16/kernel_api.h:7-29).
+template <int G, int V>
+__global__ void __launch_bounds__(kThreads) layernorm_rows(const uint4* __restrict__ x,
+                                                           const float* __restrict__ w,
+                                                           const float* __restrict__ b,
+                                                           uint4* __restrict__ y, int64_t R,
+                                                           float eps) {
+  constexpr int C = G * V * 8;
+  __shared__ float red[kThreads / 32];
+  const RowWalk<G> rw;
+  uint4 nxt[V];
+  if (rw.first + rw.sub < R) row_load<G, V>(nxt, x, rw.first + rw.sub, rw.g);
+  for (int64_t base = rw.first; base < R; base += rw.step) {
+    const int64_t r = base + rw.sub;
+    float v[V][8];
+    unpack_rows<V>(v, nxt);
+    if (r + rw.step < R) row_load<G, V>(nxt, x, r + rw.step, rw.g);
     float s = 0.f;
 #pragma unroll
-    for (int j = 0; j < VPL; ++j)
+    for (int j = 0; j < V; ++j)
 #pragma unroll
       for (int q = 0; q < 8; ++q) s += v[j][q];
-    const float mean = warp_sum(s) * (1.0f / C);
+    const float mean = row_sum<G>(s, red) * (1.0f / C);
     float ss = 0.f;
 #pragma unroll
-    for (int j = 0; j < VPL; ++j)
+    for (int j = 0; j < V; ++j)
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         const float d = v[j][q] - mean;
         ss += d * d;
       }
-    const float var = warp_sum(ss) * (1.0f / C);
+    const float var = row_sum<G>(ss, red) * (1.0f / C);
     const float inv = 1.0f / sqrtf(var + eps);
-    uint4* yr = y + r * (C / 8);
+    if (r < R) {
 #pragma unroll
-    for (int j = 0; j < VPL; ++j) {
-      const int c0 = (j * 32 + lane) * 8;
-      const float4 w0 = __ldg(reinterpret_cast<const float4*>(w + c0));
-      const float4 w1 = __ldg(reinterpret_cast<const float4*>(w + c0 + 4));
-      const float4 b0 = __ldg(reinterpret_cast<const float4*>(b + c0));
-      const float4 b1 = __ldg(reinterpret_cast<const float4*>(b + c0 + 4));
-      const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-      const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-      H8 o;
+      for (int j = 0; j < V; ++j) {
+        const int c0 = (j * G + rw.g) * 8;
+        const float4 w0 = __ldg(reinterpret_cast<const float4*>(w + c0));
+        const float4 w1 = __ldg(reinterpret_cast<const float4*>(w + c0 + 4));
+        const float4 b0 = __ldg(reinterpret_cast<const float4*>(b + c0));
+        const float4 b1 = __ldg(reinterpret_cast<const float4*>(b + c0 + 4));
+        const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+        H8 o;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float o0 = (v[j][2 * q] - mean) * inv * ww[2 * q] + bb[2 * q];
-        const float o1 =
-            (v[j][2 * q + 1] - mean) * inv * ww[2 * q + 1] + bb[2 * q + 1];
-        o.h2[q] = __floats2half2_rn(o0, o1);
+        for (int q = 0; q < 4; ++q)
+          o.h2[q] = __floats2half2_rn((v[j][2 * q] - mean) * inv * ww[2 * q] + bb[2 * q],
+                                      (v[j][2 * q + 1] - mean) * inv * ww[2 * q + 1] +
+                                          bb[2 * q + 1]);
+        y[r * (G * V) + j * G + rw.g] = o.u;
       }
-      yr[j * 32 + lane] = o.u;
     }
   }
 }
+
+// rmsnorm: y = fp16(x * (1/sqrt(mean(x^2) + eps)) * w), w fp16
+// (kernels/rmsnorm_fp16/kernel_api.h:8-14).
+template <int G, int V>
+__global__ void __launch_bounds__(kThreads) rmsnorm_rows(const uint4* __restrict__ x,
+                                                         const uint4* __restrict__ w,
+                                                         uint4* __restrict__ y, int64_t R,
+                                                         float eps) {
+  constexpr int C = G * V * 8;
+  __shared__ float red[kThreads / 32];
+  const RowWalk<G> rw;
+  uint4 nxt[V];
+  if (rw.first + rw.sub < R) row_load<G, V>(nxt, x, rw.first + rw.sub, rw.g);
+  for (int64_t base = rw.first; base < R; base += rw.step) {
+    const int64_t r = base + rw.sub;
+    float v[V][8];
+    unpack_rows<V>(v, nxt);
+    if (r + rw.step < R) row_load<G, V>(nxt, x, r + rw.step, rw.g);
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < V; ++j)
+#pragma unroll
+      for (int q = 0; q < 8; ++q) ss += v[j][q] * v[j][q];
+    const float inv = 1.0f / sqrtf(row_sum<G>(ss, red) * (1.0f / C) + eps);
+    if (r < R) {
+#pragma unroll
+      for (int j = 0; j < V; ++j) {
+        H8 hw, o;
+        hw.u = __ldg(w + j * G + rw.g);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 fw = __half22float2(hw.h2[q]);
+          o.h2[q] = __floats2half2_rn(v[j][2 * q] * inv * fw.x, v[j][2 * q + 1] * inv * fw.y);
+        }
+        y[r * (G * V) + j * G + rw.g] = o.u;
+      }
+    }
+  }
+}
+
+// softmax: max, exp of the shifted values, sum, divide; fp32 throughout and
+// one rounding (kernels/softmax_fp16/kernel_api.h:9-16).
+template <int G, int V>
+__global__ void __launch_bounds__(kThreads) softmax_rows(const uint4* __restrict__ x,
+                                                         uint4* __restrict__ y, int64_t R) {
+  __shared__ float red[kThreads / 32];
+  const RowWalk<G> rw;
+  uint4 nxt[V];
+  if (rw.first + rw.sub < R) row_load<G, V>(nxt, x, rw.first + rw.sub, rw.g);
+  for (int64_t base = rw.first; base < R; base += rw.step) {
+    const int64_t r = base + rw.sub;
+    float v[V][8];
+    unpack_rows<V>(v, nxt);
+    if (r + rw.step < R) row_load<G, V>(nxt, x, r + rw.step, rw.g);
+    float m = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < V; ++j)
+#pragma unroll
+      for (int q = 0; q < 8; ++q) m = fmaxf(m, v[j][q]);
+    m = row_max<G>(m, red);
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < V; ++j)
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        v[j][q] = expf(v[j][q] - m);
+        s += v[j][q];
+      }
+    const float sum = row_sum<G>(s, red);
+    if (r < R) {
+#pragma unroll
+      for (int j = 0; j < V; ++j) {
+        H8 o;
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          o.h2[q] = __floats2half2_rn(v[j][2 * q] / sum, v[j][2 * q + 1] / sum);
+        y[r * (G * V) + j * G + rw.g] = o.u;
+      }
+    }
+  }
+}
+
+// Any C: one warp per row, three passes over global memory.
 
 // Any C: one warp per row, three passes over global memory.
 __global__ void layernorm_f16_generic(const __half* __restrict__ x,
@@ -299,51 +455,6 @@ __global__ void layernorm_f16_generic(const __half* __restrict__ x,
   }
 }
 
-// ---- rmsnorm -------------------------------------------------------------------
-// y = fp16(x * (1/sqrt(mean(x^2) + eps)) * w), w fp16
-// (kernels/rmsnorm_fp16/kernel_api.h:8-14).
-
-template <int VPL>
-__global__ void rmsnorm_f16_reg(const uint4* __restrict__ x,
-                                const uint4* __restrict__ w,
-                                uint4* __restrict__ y, int64_t R, float eps) {
-  constexpr int C = VPL * 256;
-  const int lane = threadIdx.x & 31;
-  const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
-  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  for (int64_t r = warp0; r < R; r += nwarps) {
-    const uint4* xr = x + r * (C / 8);
-    float v[VPL][8];
-    float ss = 0.f;
-#pragma unroll
-    for (int j = 0; j < VPL; ++j) {
-      H8 h;
-      h.u = __ldg(xr + j * 32 + lane);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        float2 f = __half22float2(h.h2[q]);
-        v[j][2 * q] = f.x;
-        v[j][2 * q + 1] = f.y;
-        ss += f.x * f.x + f.y * f.y;
-      }
-    }
-    const float inv = 1.0f / sqrtf(warp_sum(ss) * (1.0f / C) + eps);
-    uint4* yr = y + r * (C / 8);
-#pragma unroll
-    for (int j = 0; j < VPL; ++j) {
-      H8 hw, o;
-      hw.u = __ldg(w + j * 32 + lane);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float2 fw = __half22float2(hw.h2[q]);
-        o.h2[q] = __floats2half2_rn(v[j][2 * q] * inv * fw.x,
-                                    v[j][2 * q + 1] * inv * fw.y);
-      }
-      yr[j * 32 + lane] = o.u;
-    }
-  }
-}
-
 __global__ void rmsnorm_f16_generic(const __half* __restrict__ x,
                                     const __half* __restrict__ w,
                                     __half* __restrict__ y, int64_t R, int C,
@@ -362,56 +473,6 @@ __global__ void rmsnorm_f16_generic(const __half* __restrict__ x,
     for (int c = lane; c < C; c += 32)
       y[r * C + c] =
           __float2half_rn(__half2float(xr[c]) * inv * __half2float(w[c]));
-  }
-}
-
-// ---- softmax --------------------------------------------------------------------
-// Row softmax: max, exp of the shifted values, sum, divide; fp32 throughout
-// and one rounding (kernels/softmax_fp16/kernel_api.h:9-16). One warp per
-// row with the row in registers for C = 256 * VPL.
-
-template <int VPL>
-__global__ void softmax_f16_reg(const uint4* __restrict__ x,
-                                uint4* __restrict__ y, int64_t R) {
-  constexpr int C = VPL * 256;
-  const int lane = threadIdx.x & 31;
-  const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
-  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  for (int64_t r = warp0; r < R; r += nwarps) {
-    const uint4* xr = x + r * (C / 8);
-    float v[VPL][8];
-    float m = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < VPL; ++j) {
-      H8 h;
-      h.u = __ldg(xr + j * 32 + lane);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        float2 f = __half22float2(h.h2[q]);
-        v[j][2 * q] = f.x;
-        v[j][2 * q + 1] = f.y;
-        m = fmaxf(m, fmaxf(f.x, f.y));
-      }
-    }
-    m = warp_max(m);
-    float s = 0.f;
-#pragma unroll
-    for (int j = 0; j < VPL; ++j)
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        v[j][q] = expf(v[j][q] - m);
-        s += v[j][q];
-      }
-    const float sum = warp_sum(s);
-    uint4* yr = y + r * (C / 8);
-#pragma unroll
-    for (int j = 0; j < VPL; ++j) {
-      H8 o;
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        o.h2[q] = __floats2half2_rn(v[j][2 * q] / sum, v[j][2 * q + 1] / sum);
-      yr[j * 32 + lane] = o.u;
-    }
   }
 }
 
@@ -649,6 +710,52 @@ __global__ void transpose_hd_tiled(const __half* __restrict__ x,
   }
 }
 
+// Vector form (T % 8 == 0, D % 8 == 0, 16-byte aligned): 16-byte loads of 8
+// consecutive d of one t, 16-byte stores of 8 consecutive t of one d. The
+// 64 x 64 tile sits in shared memory as 64 rows of t, its 16-byte chunks
+// XOR-swizzled by (t >> 3) & 7: a quarter-warp's row write touches 8
+// distinct chunks, and the column gather of eight threads that share d but
+// not t >> 3 reads 8 distinct chunks -- no bank conflicts either way.
+__global__ void transpose_hd_vec(const uint4* __restrict__ x, uint4* __restrict__ y,
+                                 int64_t B, int T, int D) {
+  __shared__ __align__(16) __half tile[kTile * kTile];
+  const int tiles_t = (T + kTile - 1) / kTile;
+  const int tiles_d = (D + kTile - 1) / kTile;
+  const int64_t ntiles = B * tiles_t * tiles_d;
+  const int dv = D / 8, tv = T / 8;              // uint4 per input row / output row
+  for (int64_t tid = blockIdx.x; tid < ntiles; tid += gridDim.x) {
+    const int64_t b = tid / ((int64_t)tiles_t * tiles_d);
+    const int rem = (int)(tid - b * tiles_t * tiles_d);
+    const int t0 = (rem / tiles_d) * kTile;
+    const int d0 = (rem % tiles_d) * kTile;
+    const uint4* xb = x + b * (int64_t)T * dv;
+    uint4* yb = y + b * (int64_t)D * tv;
+    // 512 chunks: (row t, chunk c of 8 d)
+#pragma unroll
+    for (int e = threadIdx.x; e < kTile * 8; e += kThreads) {
+      const int tr = e >> 3, c = e & 7;
+      const int t = t0 + tr, d = d0 + c * 8;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (t < T && d < D) v = __ldg(xb + (int64_t)t * dv + d / 8);
+      *reinterpret_cast<uint4*>(&tile[tr * kTile + ((c ^ ((tr >> 3) & 7)) * 8)]) = v;
+    }
+    __syncthreads();
+    // 512 outputs: (row d, chunk t8 of 8 t); eight consecutive threads cover
+    // one d row's 64 t, so a warp stores four 128-byte row segments
+#pragma unroll
+    for (int e = threadIdx.x; e < kTile * 8; e += kThreads) {
+      const int dr = e >> 3, t8 = e & 7;
+      const int d = d0 + dr, t = t0 + t8 * 8;
+      const int c = dr >> 3, w = dr & 7;
+      __align__(16) __half h[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) h[i] = tile[(t8 * 8 + i) * kTile + ((c ^ t8) * 8) + w];
+      if (d < D && t < T) yb[(int64_t)d * tv + t / 8] = *reinterpret_cast<const uint4*>(h);
+    }
+    __syncthreads();
+  }
+}
+
 // ---- patchify ---------------------------------------------------------------------
 // [C,T,H,W] -> [gh*gw, C*T*p*p] in merge-block token order
 // (kernels/patchify_fp32/kernel_api.h:18-38; structural.py:172-207):
@@ -739,19 +846,12 @@ int memory_kernels_init() {
       (const void*)scale_f16_vec,       (const void*)scale_f16_scalar,
       (const void*)cast_f32_f16_vec,    (const void*)cast_f32_f16_scalar,
       (const void*)copy_vec,            (const void*)copy_bytes,
-      (const void*)layernorm_f16_reg<1>, (const void*)layernorm_f16_reg<2>,
-      (const void*)layernorm_f16_reg<3>, (const void*)layernorm_f16_reg<4>,
-      (const void*)layernorm_f16_generic,
-      (const void*)rmsnorm_f16_reg<1>,  (const void*)rmsnorm_f16_reg<2>,
-      (const void*)rmsnorm_f16_reg<3>,  (const void*)rmsnorm_f16_reg<4>,
-      (const void*)rmsnorm_f16_reg<16>, (const void*)rmsnorm_f16_generic,
-      (const void*)softmax_f16_reg<1>,  (const void*)softmax_f16_reg<2>,
-      (const void*)softmax_f16_reg<3>,  (const void*)softmax_f16_reg<4>,
-      (const void*)softmax_f16_reg<8>,  (const void*)softmax_f16_reg<16>,
+      (const void*)layernorm_f16_generic, (const void*)rmsnorm_f16_generic,
       (const void*)softmax_f16_generic, (const void*)rope_f16_vec,
       (const void*)rope_f16_scalar,     (const void*)transpose_th_vec,
       (const void*)rope_qk_vec,
       (const void*)transpose_th_scalar, (const void*)transpose_hd_tiled,
+      (const void*)transpose_hd_vec,
       (const void*)patchify_vec,        (const void*)patchify_scalar,
   };
   for (const void* f : fns) {
@@ -762,21 +862,27 @@ int memory_kernels_init() {
     }
   }
   grid_for(1, kThreads);
-  const void* ln[5] = {nullptr, (const void*)layernorm_f16_reg<1>,
-                       (const void*)layernorm_f16_reg<2>, (const void*)layernorm_f16_reg<3>,
-                       (const void*)layernorm_f16_reg<4>};
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  for (int v = 1; v <= 4; ++v) {
+  auto note = [&](const void* f) {
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, ln[v], kThreads, 0) !=
-        cudaSuccess) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, f, kThreads, 0) != cudaSuccess) {
       cudaGetLastError();
       per_sm = 0;
     }
-    g_ln_resident[v] = per_sm * sms;
-  }
+    g_resident[f] = per_sm * sms;
+  };
+#define HB_NOTE_ROWS(K)                                                             \
+  note((const void*)K<8, 1>); note((const void*)K<16, 1>); note((const void*)K<32, 1>); \
+  note((const void*)K<32, 2>); note((const void*)K<32, 3>); note((const void*)K<32, 4>); \
+  note((const void*)K<256, 1>); note((const void*)K<256, 2>); note((const void*)K<256, 4>);
+  HB_NOTE_ROWS(layernorm_rows)
+  HB_NOTE_ROWS(rmsnorm_rows)
+  HB_NOTE_ROWS(softmax_rows)
+#undef HB_NOTE_ROWS
+  for (const auto& kv : g_resident)
+    if (kv.second <= 0) return HEXLIB_B200_ERR_CUDA;
   return HEXLIB_B200_OK;
 }
 
@@ -866,32 +972,61 @@ int launch_copy(const void* x, void* y, int64_t nbytes, cudaStream_t s) {
   HB_LAUNCH_CHECK();
 }
 
+// The (G, V) row layout for a row of C fp16 (C = G * V * 8), or {0, 0}.
+struct RowCfg {
+  int g, v;
+};
+
+RowCfg row_cfg(int C) {
+  if (C % 8) return {0, 0};
+  switch (C / 8) {
+    case 8: return {8, 1};
+    case 16: return {16, 1};
+    case 32: return {32, 1};
+    case 64: return {32, 2};
+    case 96: return {32, 3};
+    case 128: return {32, 4};
+    case 256: return {256, 1};
+    case 512: return {256, 2};
+    case 1024: return {256, 4};
+  }
+  return {0, 0};
+}
+
+// Launch a row kernel on no more CTAs than stay resident or have rows to do.
+template <class F, class... A>
+int launch_rows(F* kern, int g, int64_t R, cudaStream_t s, A... args) {
+  const int64_t rows_per_cta = g <= 32 ? (kThreads / 32) * (32 / g) : 1;
+  const int64_t need = (R + rows_per_cta - 1) / rows_per_cta;
+  auto it = g_resident.find((const void*)kern);
+  int64_t grid = (it != g_resident.end() && it->second > 0) ? it->second : need;
+  if (grid > need) grid = need;
+  kern<<<(int)grid, kThreads, 0, s>>>(args...);
+  HB_LAUNCH_CHECK();
+}
+
+#define HB_ROW_SWITCH(K, cfg, R, s, ...)                                           \
+  switch (cfg.g * 16 + cfg.v) {                                                    \
+    case 8 * 16 + 1: return launch_rows(K<8, 1>, 8, R, s, __VA_ARGS__);            \
+    case 16 * 16 + 1: return launch_rows(K<16, 1>, 16, R, s, __VA_ARGS__);         \
+    case 32 * 16 + 1: return launch_rows(K<32, 1>, 32, R, s, __VA_ARGS__);         \
+    case 32 * 16 + 2: return launch_rows(K<32, 2>, 32, R, s, __VA_ARGS__);         \
+    case 32 * 16 + 3: return launch_rows(K<32, 3>, 32, R, s, __VA_ARGS__);         \
+    case 32 * 16 + 4: return launch_rows(K<32, 4>, 32, R, s, __VA_ARGS__);         \
+    case 256 * 16 + 1: return launch_rows(K<256, 1>, 256, R, s, __VA_ARGS__);      \
+    case 256 * 16 + 2: return launch_rows(K<256, 2>, 256, R, s, __VA_ARGS__);      \
+    case 256 * 16 + 4: return launch_rows(K<256, 4>, 256, R, s, __VA_ARGS__);      \
+  }
+
 int launch_layernorm_f16(const void* x, const float* w, const float* b,
                          void* y, int64_t R, int C, float eps, cudaStream_t s) {
   if (R < 0 || C <= 0) return HEXLIB_B200_ERR_INVAL_PARAMS;
   if (R == 0) return HEXLIB_B200_OK;
   const bool al = aligned16(x) && aligned16(y) && aligned16(w) && aligned16(b);
-  int grid = grid_for(R * 32, kThreads);
-  // The register kernels loop over rows: launch only as many CTAs as stay
-  // resident, so every warp keeps its two rows of loads in flight.
-  const int vpl = (C % 256 == 0 && C <= 1024) ? C / 256 : 0;
-  if (al && vpl > 0 && g_ln_resident[vpl] > 0 && grid > g_ln_resident[vpl])
-    grid = g_ln_resident[vpl];
-  if (al && C == 256)
-    layernorm_f16_reg<1><<<grid, kThreads, 0, s>>>(
-        (const uint4*)x, w, b, (uint4*)y, R, eps);
-  else if (al && C == 512)
-    layernorm_f16_reg<2><<<grid, kThreads, 0, s>>>(
-        (const uint4*)x, w, b, (uint4*)y, R, eps);
-  else if (al && C == 768)
-    layernorm_f16_reg<3><<<grid, kThreads, 0, s>>>(
-        (const uint4*)x, w, b, (uint4*)y, R, eps);
-  else if (al && C == 1024)
-    layernorm_f16_reg<4><<<grid, kThreads, 0, s>>>(
-        (const uint4*)x, w, b, (uint4*)y, R, eps);
-  else
-    layernorm_f16_generic<<<grid, kThreads, 0, s>>>(
-        (const __half*)x, w, b, (__half*)y, R, C, eps);
+  const RowCfg cfg = al ? row_cfg(C) : RowCfg{0, 0};
+  HB_ROW_SWITCH(layernorm_rows, cfg, R, s, (const uint4*)x, w, b, (uint4*)y, R, eps)
+  layernorm_f16_generic<<<grid_for(R * 32, kThreads), kThreads, 0, s>>>(
+      (const __half*)x, w, b, (__half*)y, R, C, eps);
   HB_LAUNCH_CHECK();
 }
 
@@ -900,25 +1035,10 @@ int launch_rmsnorm_f16(const void* x, const void* w, void* y, int64_t R, int C,
   if (R < 0 || C <= 0) return HEXLIB_B200_ERR_INVAL_PARAMS;
   if (R == 0) return HEXLIB_B200_OK;
   const bool al = aligned16(x) && aligned16(y) && aligned16(w);
-  const int grid = grid_for(R * 32, kThreads);
-  if (al && C == 256)
-    rmsnorm_f16_reg<1><<<grid, kThreads, 0, s>>>(
-        (const uint4*)x, (const uint4*)w, (uint4*)y, R, eps);
-  else if (al && C == 512)
-    rmsnorm_f16_reg<2><<<grid, kThreads, 0, s>>>(
-        (const uint4*)x, (const uint4*)w, (uint4*)y, R, eps);
-  else if (al && C == 768)
-    rmsnorm_f16_reg<3><<<grid, kThreads, 0, s>>>(
-        (const uint4*)x, (const uint4*)w, (uint4*)y, R, eps);
-  else if (al && C == 1024)
-    rmsnorm_f16_reg<4><<<grid, kThreads, 0, s>>>(
-        (const uint4*)x, (const uint4*)w, (uint4*)y, R, eps);
-  else if (al && C == 4096)
-    rmsnorm_f16_reg<16><<<grid, kThreads, 0, s>>>(
-        (const uint4*)x, (const uint4*)w, (uint4*)y, R, eps);
-  else
-    rmsnorm_f16_generic<<<grid, kThreads, 0, s>>>(
-        (const __half*)x, (const __half*)w, (__half*)y, R, C, eps);
+  const RowCfg cfg = al ? row_cfg(C) : RowCfg{0, 0};
+  HB_ROW_SWITCH(rmsnorm_rows, cfg, R, s, (const uint4*)x, (const uint4*)w, (uint4*)y, R, eps)
+  rmsnorm_f16_generic<<<grid_for(R * 32, kThreads), kThreads, 0, s>>>(
+      (const __half*)x, (const __half*)w, (__half*)y, R, C, eps);
   HB_LAUNCH_CHECK();
 }
 
@@ -927,23 +1047,10 @@ int launch_softmax_f16(const void* x, void* y, int64_t R, int C,
   if (R < 0 || C <= 0) return HEXLIB_B200_ERR_INVAL_PARAMS;
   if (R == 0) return HEXLIB_B200_OK;
   const bool al = aligned16(x) && aligned16(y);
-  const int grid = grid_for(R * 32, kThreads);
-  if (al && C == 256)
-    softmax_f16_reg<1><<<grid, kThreads, 0, s>>>((const uint4*)x, (uint4*)y, R);
-  else if (al && C == 512)
-    softmax_f16_reg<2><<<grid, kThreads, 0, s>>>((const uint4*)x, (uint4*)y, R);
-  else if (al && C == 768)
-    softmax_f16_reg<3><<<grid, kThreads, 0, s>>>((const uint4*)x, (uint4*)y, R);
-  else if (al && C == 1024)
-    softmax_f16_reg<4><<<grid, kThreads, 0, s>>>((const uint4*)x, (uint4*)y, R);
-  else if (al && C == 2048)
-    softmax_f16_reg<8><<<grid, kThreads, 0, s>>>((const uint4*)x, (uint4*)y, R);
-  else if (al && C == 4096)
-    softmax_f16_reg<16><<<grid, kThreads, 0, s>>>((const uint4*)x, (uint4*)y,
-                                                   R);
-  else
-    softmax_f16_generic<<<grid, kThreads, 0, s>>>((const __half*)x, (__half*)y,
-                                                  R, C);
+  const RowCfg cfg = al ? row_cfg(C) : RowCfg{0, 0};
+  HB_ROW_SWITCH(softmax_rows, cfg, R, s, (const uint4*)x, (uint4*)y, R)
+  softmax_f16_generic<<<grid_for(R * 32, kThreads), kThreads, 0, s>>>((const __half*)x,
+                                                                      (__half*)y, R, C);
   HB_LAUNCH_CHECK();
 }
 
@@ -1007,8 +1114,10 @@ int launch_transpose_hd_f16(const void* x, void* y, int64_t B, int T, int D,
   const int64_t ntiles =
       B * ((T + kTile - 1) / kTile) * (int64_t)((D + kTile - 1) / kTile);
   int grid = grid_for(ntiles * kThreads, kThreads);
-  transpose_hd_tiled<<<grid, kThreads, 0, s>>>((const __half*)x, (__half*)y, B,
-                                               T, D);
+  if (T % 8 == 0 && D % 8 == 0 && aligned16(x) && aligned16(y))
+    transpose_hd_vec<<<grid, kThreads, 0, s>>>((const uint4*)x, (uint4*)y, B, T, D);
+  else
+    transpose_hd_tiled<<<grid, kThreads, 0, s>>>((const __half*)x, (__half*)y, B, T, D);
   HB_LAUNCH_CHECK();
 }
 

@@ -92,7 +92,12 @@ def test_cast_rounds_to_nearest_even(n):
 
 # ---- rows -------------------------------------------------------------------
 
-@pytest.mark.parametrize("R,C", [(256, 768), (4, 64), (3, 1000), (2, 256), (5, 1024)])
+@pytest.mark.parametrize("R,C", [
+    (256, 768), (4, 64), (3, 1000), (2, 256), (5, 1024),
+    (4100, 64), (37, 128),            # 8 and 16 lanes per row, rows ending mid-warp
+    (3, 2048), (5, 4096), (2, 8192),  # a CTA per row
+    (4100, 768), (5000, 256), (4099, 512), (4096, 1024),  # many rows per warp, ragged end
+])
 def test_layernorm(R, C):
     x = randn16((R, C), 8)
     w = (1.0 + rng(9).standard_normal(C) * 0.02).astype(np.float32)
@@ -121,7 +126,8 @@ def test_layernorm_distinguishes_biased_variance():
     assert_close_f16(got, oracle16("layernorm", (x, w, b), {"eps": 1e-6}), what="layernorm C=64")
 
 
-@pytest.mark.parametrize("R,C", [(256, 768), (8, 128), (3, 4096), (2, 100)])
+@pytest.mark.parametrize("R,C", [(256, 768), (8, 128), (3, 4096), (2, 100),
+                                 (4100, 64), (3, 2048), (2, 8192)])
 def test_rmsnorm(R, C):
     x = randn16((R, C), 12)
     w = f16(1.0 + rng(13).standard_normal(C) * 0.1)
@@ -131,7 +137,8 @@ def test_rmsnorm(R, C):
     assert_close_f16(G.host(y), oracle16("rmsnorm", (x, w), {"eps": 1e-5}), what="rmsnorm")
 
 
-@pytest.mark.parametrize("R,C", [(12 * 256, 256), (6, 256), (64, 1024), (4, 4096), (5, 1000), (3, 33)])
+@pytest.mark.parametrize("R,C", [(12 * 256, 256), (6, 256), (64, 1024), (4, 4096), (5, 1000),
+                                 (3, 33), (4100, 64), (37, 128), (3, 2048), (2, 8192)])
 def test_softmax(R, C):
     x = randn16((R, C), 14, scale=3.0)
     if R >= 2:
@@ -171,7 +178,10 @@ def test_transpose_th_is_bit_exact(T, H, D):
     assert_bit_exact(G.host(y), np.ascontiguousarray(x.transpose(1, 0, 2)), "transpose_th")
 
 
-@pytest.mark.parametrize("B,T,D", [(12, 256, 64), (5, 64, 7), (5, 40, 7), (3, 130, 70)])
+@pytest.mark.parametrize("B,T,D", [
+    (12, 256, 64), (2, 4096, 64),     # 16-byte path, whole tiles
+    (3, 200, 72), (2, 72, 136),       # 16-byte path, partial t and d tiles
+    (5, 64, 7), (5, 40, 7), (3, 130, 70)])   # element path
 def test_transpose_hd_is_bit_exact(B, T, D):
     x = randn16((B, T, D), 18)
     y = G.empty((B, D, T), np.float16)
