@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--no-attention-fusion", action="store_true")
     ap.add_argument("--no-residual-fusion", action="store_true")
     ap.add_argument("--no-qkv-fusion", action="store_true")
+    ap.add_argument("--weights", choices=("fp16", "q4_0", "q8_0"), default="fp16",
+                    help="matmul weight dtype (q4_0 is the reference model's own)")
     ap.add_argument("--sweep", action="store_true",
                     help="instead of the encoder: the memory-bound kernel sweep (one GPU), "
                          "one JSON line per kernel and shape")
@@ -266,7 +268,7 @@ def run_b200(args) -> None:
                                 device_id=torch.device("cuda", local))
         pg = dist
 
-    cfg = G.qwen35_at(args.image_size)
+    cfg = G.qwen35_at(args.image_size, weight_dtype=args.weights)
     g = G.build_vision_encoder(cfg)
     use_att = (not args.no_attention_fusion) and attention_available()
     use_qkv = use_att and not args.no_qkv_fusion
@@ -424,10 +426,10 @@ def run_b200(args) -> None:
                             f"global batch {args.batch}, sharded by image",
                 "image_size": cfg.image_size, "global_batch": args.batch,
                 "seq_len": cfg.num_tokens, "parallelism": f"image-sharded x{world}",
-                "plan_ops": plan.n_ops, "fusions": {"attention": use_att, "qkv_rope": use_qkv,
+                "weights": args.weights, "plan_ops": plan.n_ops, "fusions": {"attention": use_att, "qkv_rope": use_qkv,
                                                    "residual": not args.no_residual_fusion},
-                "l2": "inputs larger than L2: each step reads 201 MB of weights and "
-                      f"{n * 6.29:.0f} MB of images per GPU",
+                "l2": f"inputs larger than L2: each step reads {plan.const_bytes / 1e6:.0f} MB "
+                      f"of consts and {n * 6.29:.0f} MB of images per GPU",
             },
             "e2e": {"value": e2e, "unit": UNIT,
                     "h2d_bytes_per_step": int(host_in.numel() * 4),

@@ -128,7 +128,15 @@ int need(const OpRec& op, uint32_t nbuf) {
   for (uint32_t i = 0; i < nbuf; ++i) {
     if (op.a[i].layout != LAYOUT_ROW_MAJOR) return HEXLIB_B200_ERR_REQUIRES;
     const int es = esize(op.a[i].dtype);
-    if (es == 0) return HEXLIB_B200_ERR_REQUIRES;
+    if (es == 0) {
+      // q4_0 / q8_0: blocks of 32 along the last axis (ir.py nbytes)
+      const int bb = hb::quant_block_bytes((int)op.a[i].dtype);
+      if (bb == 0) return HEXLIB_B200_ERR_REQUIRES;
+      const uint64_t n = numel(op.a[i].ne);
+      if (n % 32 || (n / 32) * (uint64_t)bb != op.a[i].nbytes)
+        return HEXLIB_B200_ERR_INVAL_PARAMS;
+      continue;
+    }
     if (numel(op.a[i].ne) * (uint64_t)es != op.a[i].nbytes)
       return HEXLIB_B200_ERR_INVAL_PARAMS;
   }
@@ -313,7 +321,10 @@ int check_op(const OpRec& op) {
       const uint32_t nb = res ? 5 : 4;
       HB_TRY(need(op, nb));
       HB_TRY(dt(op, 0, DT_FP16));
-      HB_TRY(dt(op, 1, DT_FP16));  // the reference's q4_0 weight is refused here
+      // the weight: fp16, or the reference's q4_0 (or q8_0), blocks along N
+      const uint32_t wdt = op.a[1].dtype;
+      if (wdt != DT_FP16 && wdt != DT_Q4_0 && wdt != DT_Q8_0) return HEXLIB_B200_ERR_REQUIRES;
+      if (wdt != DT_FP16 && op.a[1].ne[1] % 32) return HEXLIB_B200_ERR_INVAL_PARAMS;
       HB_TRY(dt(op, 2, DT_FP32));
       if (res) HB_TRY(dt(op, 3, DT_FP16));
       HB_TRY(dt(op, nb - 1, DT_FP16));
@@ -405,7 +416,10 @@ int check_op(const OpRec& op) {
 }
 
 // Enqueue one validated op for n images. Returns a status.
-int run_op(const OpRec& op, uint32_t n_images, int* err, cudaStream_t s) {
+// `ws`: the session's scratch for dequantized weights (ws_bytes, sized by
+// ensure_workspace before any op of the batch is launched or captured).
+int run_op(const OpRec& op, uint32_t n_images, int* err, void* ws, uint64_t ws_bytes,
+           cudaStream_t s) {
   bool batched = false;
   for (uint32_t i = 0; i < op.nbuf; ++i) batched = batched || op.a[i].per_image;
   const int64_t B = batched ? n_images : 1;
@@ -496,6 +510,8 @@ int run_op(const OpRec& op, uint32_t n_images, int* err, cudaStream_t s) {
       g.N = (int)a[1].ne[1];
       g.b_shared = true;
       g.act = op.params[0];
+      if (a[1].dtype != DT_FP16)
+        return hb::launch_gemm_quant(g, (int)a[1].dtype, ws, ws_bytes, err, s);
       return hb::launch_gemm(g, err, s);
     }
     case HEXLIB_B200_KIND_MATMUL_EPILOGUE_ROPE: {
@@ -703,6 +719,9 @@ struct hexlib_b200_ctx {
   int* err_host = nullptr;
   int* err_dev = nullptr;
   uint64_t mapped = 0;
+  // scratch for the fp16 copy of a quantized weight, one op at a time
+  void* ws = nullptr;
+  uint64_t ws_bytes = 0;
 };
 
 namespace {
@@ -780,7 +799,8 @@ int run_eager(hexlib_b200_ctx* ctx, const Parsed& p, uint32_t n,
   cudaEventRecord(ctx->ev0, ctx->stream);
   if (timed && n) cudaEventRecord(ctx->op_events[0], ctx->stream);
   for (uint32_t i = 0; i < n; ++i) {
-    const int rc = run_op(p.ops[i], n_images, ctx->err_dev, ctx->stream);
+    const int rc = run_op(p.ops[i], n_images, ctx->err_dev, ctx->ws, ctx->ws_bytes,
+                          ctx->stream);
     if (rc != HEXLIB_B200_OK) {
       *fail_status = rc;
       break;
@@ -870,6 +890,38 @@ static void drop_graphs(hexlib_b200_ctx* ctx) {
   ctx->graphs.clear();
 }
 
+// Grow the quantized-weight scratch to what this batch's ops need. Done on
+// the host before any of the batch is launched or captured; growing it frees
+// the old block, so every cached graph (which holds its address) is dropped.
+static int ensure_workspace(hexlib_b200_ctx* ctx, const Parsed& p) {
+  uint64_t need = 0;
+  for (const OpRec& op : p.ops) {
+    if ((op.kind == HEXLIB_B200_KIND_MATMUL_EPILOGUE ||
+         op.kind == HEXLIB_B200_KIND_MATMUL_EPILOGUE_RESIDUAL) &&
+        op.a[1].dtype != DT_FP16) {
+      const uint64_t b = (uint64_t)op.a[1].ne[0] * op.a[1].ne[1] * 2u;
+      if (b > need) need = b;
+    }
+  }
+  if (need <= ctx->ws_bytes) return HEXLIB_B200_OK;
+  need = (need + 255) & ~uint64_t(255);
+  if (cudaStreamSynchronize(ctx->stream) != cudaSuccess) {
+    cudaGetLastError();
+    return HEXLIB_B200_ERR_CUDA;
+  }
+  drop_graphs(ctx);
+  if (ctx->ws) cudaFree(ctx->ws);
+  ctx->ws = nullptr;
+  ctx->ws_bytes = 0;
+  if (cudaMalloc(&ctx->ws, need) != cudaSuccess) {
+    cudaGetLastError();
+    ctx->ws = nullptr;
+    return HEXLIB_B200_ERR_CUDA;
+  }
+  ctx->ws_bytes = need;
+  return HEXLIB_B200_OK;
+}
+
 int hexlib_b200_close(hexlib_b200_ctx* ctx) {
   if (!ctx) return HEXLIB_B200_ERR_INVAL_PARAMS;
   cudaSetDevice(ctx->device);
@@ -877,6 +929,7 @@ int hexlib_b200_close(hexlib_b200_ctx* ctx) {
   drop_graphs(ctx);
   for (auto& kv : ctx->bufs) cudaFree(kv.second.ptr);
   ctx->bufs.clear();
+  if (ctx->ws) cudaFree(ctx->ws);
   for (cudaEvent_t e : ctx->op_events) cudaEventDestroy(e);
   if (ctx->ev0) cudaEventDestroy(ctx->ev0);
   if (ctx->ev1) cudaEventDestroy(ctx->ev1);
@@ -1142,6 +1195,11 @@ int hexlib_b200_invoke_images(hexlib_b200_ctx* ctx, const uint8_t* batch,
     write_rsp_hdr(rsp, (uint32_t)rc, 0, 0);
     return rc;
   }
+  rc = ensure_workspace(ctx, p);
+  if (rc != HEXLIB_B200_OK) {
+    write_rsp_hdr(rsp, (uint32_t)rc, 0, 0);
+    return rc;
+  }
   const uint32_t n_ok = (uint32_t)p.ops.size();
   const bool complete = p.fail_status == HEXLIB_B200_OK;
 
@@ -1160,7 +1218,8 @@ int hexlib_b200_invoke_images(hexlib_b200_ctx* ctx, const uint8_t* batch,
       return HEXLIB_B200_ERR_CUDA;
     }
     for (uint32_t i = 0; i < n_ok; ++i) {
-      launch_rc = run_op(p.ops[i], n_images, ctx->err_dev, ctx->stream);
+      launch_rc = run_op(p.ops[i], n_images, ctx->err_dev, ctx->ws, ctx->ws_bytes,
+                         ctx->stream);
       if (launch_rc != HEXLIB_B200_OK) {
         failed_at = i;
         break;

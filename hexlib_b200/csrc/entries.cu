@@ -14,6 +14,7 @@ namespace hb {
 
 int memory_kernels_init();
 int gemm_kernels_init();
+int quant_kernels_init();
 int attention_kernels_init();
 int diag_kernels_init();
 
@@ -27,6 +28,7 @@ int kernels_init() {
   std::call_once(g_init_once, [] {
     int rc = memory_kernels_init();
     if (rc == HEXLIB_B200_OK) rc = gemm_kernels_init();
+    if (rc == HEXLIB_B200_OK) rc = quant_kernels_init();
     if (rc == HEXLIB_B200_OK) rc = attention_kernels_init();
     if (rc == HEXLIB_B200_OK) rc = diag_kernels_init();
     int* host = nullptr;
@@ -188,6 +190,54 @@ int hexlib_b200_matmul_epilogue_fp16(const void* a, const void* w,
   g.b_shared = true;
   g.act = act;
   return hb::launch_gemm(g, hb::default_error_word(), as_stream(stream));
+}
+
+int hexlib_b200_dequant_q4_0_fp16(const void* w, void* out, int K, int N, void* stream) {
+  HB_ENTRY_INIT();
+  if (K < 0 || N < 0) return HEXLIB_B200_ERR_INVAL_PARAMS;
+  return hb::launch_dequant_f16(hb::QTYPE_Q4_0, w, out, K, N, as_stream(stream));
+}
+
+int hexlib_b200_dequant_q8_0_fp16(const void* w, void* out, int K, int N, void* stream) {
+  HB_ENTRY_INIT();
+  if (K < 0 || N < 0) return HEXLIB_B200_ERR_INVAL_PARAMS;
+  return hb::launch_dequant_f16(hb::QTYPE_Q8_0, w, out, K, N, as_stream(stream));
+}
+
+static int matmul_epilogue_quant(int qtype, const void* a, const void* w, const float* bias,
+                                 void* out, int M, int K, int N, int act, void* workspace,
+                                 uint64_t workspace_bytes, void* stream) {
+  if (M < 0 || K <= 0 || N <= 0 || N % 32 || act < 0 || act > 2 || !bias || !w)
+    return HEXLIB_B200_ERR_INVAL_PARAMS;
+  hb::GemmDesc g{};
+  g.A = a;
+  g.B = w;
+  g.bias = bias;
+  g.out = out;
+  g.batch = 1;
+  g.M = M;
+  g.K = K;
+  g.N = N;
+  g.b_shared = true;
+  g.act = act;
+  return hb::launch_gemm_quant(g, qtype, workspace, workspace_bytes, hb::default_error_word(),
+                               as_stream(stream));
+}
+
+int hexlib_b200_matmul_epilogue_q4_0(const void* a, const void* w, const float* bias,
+                                     void* out, int M, int K, int N, int act, void* workspace,
+                                     uint64_t workspace_bytes, void* stream) {
+  HB_ENTRY_INIT();
+  return matmul_epilogue_quant(hb::QTYPE_Q4_0, a, w, bias, out, M, K, N, act, workspace,
+                               workspace_bytes, stream);
+}
+
+int hexlib_b200_matmul_epilogue_q8_0(const void* a, const void* w, const float* bias,
+                                     void* out, int M, int K, int N, int act, void* workspace,
+                                     uint64_t workspace_bytes, void* stream) {
+  HB_ENTRY_INIT();
+  return matmul_epilogue_quant(hb::QTYPE_Q8_0, a, w, bias, out, M, K, N, act, workspace,
+                               workspace_bytes, stream);
 }
 
 int hexlib_b200_matmul_epilogue_residual_fp16(const void* a, const void* w,

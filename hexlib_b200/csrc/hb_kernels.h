@@ -79,6 +79,19 @@ struct GemmDesc {
 };
 int launch_gemm(const GemmDesc& g, int* err, cudaStream_t s);
 
+// Block-quantized weights (k_quant.cu). qtype is the wire dtype id of the
+// weight: QTYPE_Q4_0 (18-byte blocks) or QTYPE_Q8_0 (34-byte blocks).
+enum : int { QTYPE_Q4_0 = 2, QTYPE_Q8_0 = 4 };
+int quant_kernels_init();
+int quant_block_bytes(int qtype);  // 0 for anything else
+// [K, N] blocks along N (N % 32 == 0) -> fp16 [K, N], out 16-byte aligned.
+int launch_dequant_f16(int qtype, const void* w, void* out, int64_t K, int64_t N,
+                       cudaStream_t s);
+// g with a quantized g.B: dequantize into `workspace` (>= K*N*2 bytes), then
+// the fp16 GEMM on it. Weight shared across the batch only (b_shared, batch 1).
+int launch_gemm_quant(const GemmDesc& g, int qtype, void* workspace, uint64_t ws_bytes,
+                      int* err, cudaStream_t s);
+
 // Fused attention: q, k, v, ctx are [Bn, T, D] fp16.
 int launch_attention(const void* q, const void* k, const void* v, void* ctx,
                      int64_t Bn, int T, int D, float scale, int* err,

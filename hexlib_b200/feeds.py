@@ -8,7 +8,8 @@ workload is synthetic with the shapes and value ranges of the real one:
              mean/std the Qwen2-VL image processor uses, then duplicated along
              the temporal axis to [3, 2, S, S] fp32 (vit.py:125-129).
   weights    every const, drawn in sorted-name order from default_rng(seed):
-             fp16 2-D weights ~N(0, 0.02); LayerNorm gains 1 + N(0, 0.02);
+             fp16 2-D weights ~N(0, 0.02) (q4_0 / q8_0 ones: the same draw, left
+             dense for the batch builder to quantize); LayerNorm gains 1 + N(0, 0.02);
              biases, LayerNorm shifts and pos_embed ~N(0, 0.02) fp32.
   rope_cos/sin  the 2-D rotary tables of hexlib/models/loader.py:97-117
              (restated below), not random.
@@ -72,6 +73,10 @@ def weights(cfg: VitConfig, seed: int = 0, graph=None) -> dict[str, np.ndarray]:
             out[name] = sin
         elif t.dtype == "fp16":
             out[name] = (rng.standard_normal(t.shape, dtype=np.float32) * 0.02).astype(np.float16)
+        elif t.dtype in ("q4_0", "q8_0"):
+            # the same draw as an fp16 weight, kept dense: the batch builder
+            # quantizes it when it stages the plan
+            out[name] = (rng.standard_normal(t.shape, dtype=np.float32) * 0.02).astype(np.float32)
         elif name.endswith("ln1_w") or name.endswith("ln2_w") or name == "m_ln_w":
             out[name] = (1.0 + rng.standard_normal(t.shape, dtype=np.float32) * 0.02).astype(np.float32)
         elif t.dtype == "fp32":

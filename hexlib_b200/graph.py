@@ -526,7 +526,9 @@ def fuse_qkv(graph: Graph) -> tuple[Graph, dict[str, tuple]]:
         cos, sin = rq.inputs[1], rq.inputs[2]
         ws = [m.inputs[1] for m in mms]
         bs = [m.inputs[2] for m in mms]
-        if not all(T[w].const and T[w].dtype == "fp16" and len(T[w].shape) == 2 for w in ws):
+        wdt = T[ws[0]].dtype
+        if wdt not in ("fp16", "q4_0", "q8_0") or not all(
+                T[w].const and T[w].dtype == wdt and len(T[w].shape) == 2 for w in ws):
             continue
         if not all(T[b].const and T[b].dtype == "fp32" for b in bs):
             continue
@@ -538,7 +540,7 @@ def fuse_qkv(graph: Graph) -> tuple[Graph, dict[str, tuple]]:
         bname = f"concat({bs[0]},{bs[1]},{bs[2]})"
         raw = f"{mms[0].outputs[0]}+qkv.raw"
         qkv = f"{mms[0].outputs[0]}+qkv"
-        new_tensors[wname] = Tensor(wname, "fp16", (K, 3 * heads * d), True)
+        new_tensors[wname] = Tensor(wname, wdt, (K, 3 * heads * d), True)
         new_tensors[bname] = Tensor(bname, "fp32", (3 * heads * d,), True)
         new_tensors[raw] = Tensor(raw, "fp16", (n_tok, 3, heads, d), False)
         new_tensors[qkv] = Tensor(qkv, "fp16", (n_tok, 3, heads, d), False)

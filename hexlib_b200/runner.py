@@ -9,9 +9,10 @@ decide the variant, and `encode_params` is where attr-sourced scalars become
 the op's int32 params (floats as their IEEE-754 bits, dsp.py:286-305).
 
 DIFFERENCES FROM THE DSP's TABLE, each deliberate:
-  * matmul_epilogue takes an fp16 [K, N] weight (not q4_0): the encoder
-    configurations this backend runs use fp16 weights. A q4_0 weight on the
-    wire is refused with ERR_REQUIRES by the dispatcher's dtype guard.
+  * matmul_epilogue takes an fp16 [K, N] weight as well as the DSP's q4_0
+    one (and q8_0): a block-quantized weight is dequantized to fp16 -- every
+    value rounded as the DSP kernel rounds it -- ahead of the tensor-core
+    GEMM, in a scratch the session owns.
   * add's right operand may be fp32: the pos_embed add then rounds once,
     exactly as the numpy executor computes it, instead of pre-rounding the
     table to fp16 as the DSP spec does (runner.py:395-398).
@@ -112,6 +113,8 @@ def _norm(v):
 
 
 F16, F32 = ("fp16",), ("fp32",)
+# a matmul weight: fp16, or block-quantized (dequantized to fp16 ahead of the GEMM)
+WEIGHT = ("fp16", "q4_0", "q8_0")
 
 SPECS: dict[str, CudaSpec] = {
     "add": CudaSpec("add", (F16, ("fp16", "fp32")), "fp16", entry="hexlib_b200_add_fp16"),
@@ -120,7 +123,7 @@ SPECS: dict[str, CudaSpec] = {
     "layernorm": CudaSpec("layernorm", (F16, F32, F32), "fp16",
                           params=(Param("eps", "float"),), entry="hexlib_b200_layernorm_fp16"),
     "matmul": CudaSpec("matmul", (F16, F16), "fp16", entry="hexlib_b200_matmul_fp16"),
-    "matmul_epilogue": CudaSpec("matmul_epilogue", (F16, F16, F32), "fp16",
+    "matmul_epilogue": CudaSpec("matmul_epilogue", (F16, WEIGHT, F32), "fp16",
                                 params=(Param("act", "int", ACT_CODES),),
                                 entry="hexlib_b200_matmul_epilogue_fp16"),
     "patchify": CudaSpec("patchify", (F32,), "fp32",
@@ -142,7 +145,7 @@ SPECS: dict[str, CudaSpec] = {
     "rmsnorm": CudaSpec("rmsnorm", (F16, F16), "fp16", params=(Param("eps", "float"),),
                         entry="hexlib_b200_rmsnorm_fp16"),
     "matmul_epilogue_residual": CudaSpec(
-        "matmul_epilogue_residual", (F16, F16, F32, F16), "fp16",
+        "matmul_epilogue_residual", (F16, WEIGHT, F32, F16), "fp16",
         params=(Param("act", "int", ACT_CODES),),
         entry="hexlib_b200_matmul_epilogue_residual_fp16"),
     "matmul_epilogue_rope": CudaSpec(

@@ -29,6 +29,7 @@ from typing import Any, Mapping
 import numpy as np
 
 from hexlib_b200 import runner, wire
+from hexlib_b200 import quant
 from hexlib_b200.graph import as_graph, nbytes as ir_nbytes
 
 CONST_FD = 0
@@ -110,6 +111,22 @@ def _allocate_aliased(names, first, last, size) -> tuple[dict[str, int], int]:
         placed.append((cand, cand + sz, lo, hi))
     end = max((o + size[n] for n, o in offs.items()), default=0)
     return offs, _align(end)
+
+
+def _is_raw(v) -> bool:
+    """Packed block-quantized bytes rather than a dense value."""
+    return isinstance(v, (bytes, bytearray)) or (isinstance(v, np.ndarray) and v.dtype == np.uint8)
+
+
+def _concat_raw(parts, dtype: str, shape, axis: int) -> bytes:
+    """Concatenate packed [K, N_i] weights along N: row by row, since each row
+    of a block-quantized matrix is its own run of blocks."""
+    if axis not in (1, -1) or len(shape) != 2:
+        raise WholePlanError("packed weights concatenate only along the last axis of a matrix")
+    K = shape[0]
+    rows = [np.frombuffer(bytes(np.asarray(q, np.uint8).tobytes()) if not isinstance(q, bytes)
+                          else q, np.uint8).reshape(K, -1) for q in parts]
+    return np.concatenate(rows, axis=1).tobytes()
 
 
 def build_cuda_plan(compiled, feeds: Mapping[str, Any] | None = None,
@@ -255,11 +272,24 @@ def build_cuda_plan(compiled, feeds: Mapping[str, Any] | None = None,
                 missing = [q for q in parts if q not in feeds]
                 if missing:
                     raise WholePlanError(f"const {n!r} is built from {missing}, not supplied")
-                value = np.concatenate([np.asarray(feeds[q]) for q in parts], axis=axis)
+                if p.dtype in quant.BLOCK_BYTES and any(_is_raw(feeds[q]) for q in parts):
+                    value = _concat_raw([feeds[q] for q in parts], p.dtype, p.shape, axis)
+                else:
+                    value = np.concatenate([np.asarray(feeds[q]) for q in parts], axis=axis)
             elif n in feeds:
                 value = feeds[n]
             else:
                 raise WholePlanError(f"no feed supplied for const {n!r}")
+            if p.dtype in quant.BLOCK_BYTES:
+                # a dense weight is quantized here, as the reference's batch
+                # builder does (wholeplan.py:293-307); packed bytes pass as is
+                raw = (bytes(np.asarray(value, np.uint8).tobytes()) if _is_raw(value)
+                       else quant.quantize(np.asarray(value, np.float32), p.dtype))
+                if len(raw) != p.nbytes:
+                    raise WholePlanError(f"const {n!r}: {len(raw)} {p.dtype} bytes, "
+                                         f"declared {p.nbytes}")
+                payload[p.offset:p.offset + len(raw)] = raw
+                continue
             a = np.ascontiguousarray(np.asarray(value), dtype=_NP[p.dtype])
             if tuple(a.shape) != tuple(p.shape):
                 raise WholePlanError(f"feed {n!r} has shape {a.shape}, declared {p.shape}")

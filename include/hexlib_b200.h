@@ -242,6 +242,31 @@ HEXLIB_B200_API int hexlib_b200_matmul_fp16(const void *A, const void *B, void *
 HEXLIB_B200_API int hexlib_b200_matmul_epilogue_fp16(const void *a, const void *w,
                                      const float *bias, void *out, int M,
                                      int K, int N, int act, void *stream);
+/* The reference's own matmul_epilogue (kernels/matmul_epilogue_fp16/
+ * kernel_api.h:188-190): w is a q4_0 [K, N] weight, row-major with its
+ * 18-byte blocks of 32 along N (K any, N % 32 == 0), dequantized with every
+ * weight rounded to fp16 (baseline.c:36-47), fp32 accumulation. The kernel
+ * never allocates: the caller hands `workspace` of at least K*N*2 bytes
+ * (16-byte aligned) for the fp16 copy of the weight -- the counterpart of the
+ * VTCM scratch the reference's entry receives in hexlib_args (vtcm,
+ * vtcm_size; hexlib_dsp.h:186-198). ERR_INVAL_PARAMS when it is too small. */
+HEXLIB_B200_API int hexlib_b200_matmul_epilogue_q4_0(const void *a, const void *w,
+                                                     const float *bias, void *out, int M,
+                                                     int K, int N, int act, void *workspace,
+                                                     uint64_t workspace_bytes, void *stream);
+/* The same with a q8_0 weight (34-byte blocks: fp16 d, 32 int8; value q*d;
+ * hexlib/exec/quant.py, ir.py:26-41). No reference kernel takes q8_0 yet;
+ * the contract is q4_0's with the other block format. */
+HEXLIB_B200_API int hexlib_b200_matmul_epilogue_q8_0(const void *a, const void *w,
+                                                     const float *bias, void *out, int M,
+                                                     int K, int N, int act, void *workspace,
+                                                     uint64_t workspace_bytes, void *stream);
+/* q4_0 / q8_0 [K, N] -> fp16 [K, N] with the rounding above (w 2-byte
+ * aligned, out 16-byte aligned): the dequantization step alone. */
+HEXLIB_B200_API int hexlib_b200_dequant_q4_0_fp16(const void *w, void *out, int K, int N,
+                                                  void *stream);
+HEXLIB_B200_API int hexlib_b200_dequant_q8_0_fp16(const void *w, void *out, int K, int N,
+                                                  void *stream);
 /* matmul_epilogue followed by the residual add that consumes it
  * (hexlib/models/vit.py:196 and :203): out = act(a@w + bias) + r, with the
  * matmul result rounded to fp16 before the add, as the unfused plan does. */

@@ -23,6 +23,17 @@ repository's code in the loop:
                 build_whole_plan_batch of the tiny fp16 plan, and response
                 bytes for unpack_response.
   tables.npz    loader.rope_tables for the tiny and 256 configs.
+  quant.npz     hexlib.exec.quant's q4_0 and q8_0 bytes and dequantized values
+                for seeded blocks and the edge blocks its tests construct
+                (exact halves, positive extremes, zero blocks, the q8_0 wrap
+                case); and build_whole_plan_batch of the tiny fp16 plan --
+                whose matmul_epilogue weights the builder quantizes to q4_0 --
+                with its staged arena payload, the output's placement, and the
+                reference interpreter's output when every quantized weight is
+                replaced by its dequantized value rounded to fp16 (the
+                arithmetic the DSP kernel performs, baseline.c:36-47).
+
+`--quant-only` regenerates quant.npz alone.
 
 The fixtures are small (the biggest is well under 2 MB) and are committed;
 tests read them without the reference present.
@@ -192,5 +203,76 @@ def main(ref_root: str) -> None:
     print("wrote", sorted(os.listdir(HERE)))
 
 
+def make_quant(ref_root: str) -> None:
+    sys.path.insert(0, ref_root)
+    import hexlib.graph.opdefs  # noqa: F401
+    from hexlib.exec import interpreter
+    from hexlib.exec.quant import (dequantize_q4_0, dequantize_q8_0, quantize_q4_0,
+                                   quantize_q8_0)
+    from hexlib.exec.wholeplan import build_whole_plan_batch
+    from hexlib.graph.pipeline import compile_model
+    from hexlib.models import loader
+    from hexlib.models.vit import VitConfig, build_vision_encoder
+    from hexlib.result import Err
+
+    q = {}
+    rng = np.random.default_rng(7)
+    x = (rng.standard_normal((6, 96)) * np.array([[0.02], [1.0], [3.0], [0.5], [10.0], [1e-3]])
+         ).astype(np.float32)
+    halves = np.array([-7.5, -6.5, -5.5, -4.5, -3.5, -2.5, -1.5, -0.5,
+                       0.5, 1.5, 2.5, 3.5, 4.5, 5.5, 6.5], np.float32)
+    edge = np.zeros((4, 96), np.float32)
+    edge[0, :32] = np.concatenate([[-8.0], halves, [-8.0], halves])      # q4_0 exact halves
+    edge[0, 32:64] = np.linspace(-1, 3, 32)                               # positive extreme
+    edge[1, :32] = np.arange(32) - 15.5                                   # q8_0 halves
+    edge[1, 32:64] = np.where(np.arange(32) == 5, 1000.0, 1.0)            # extreme, d narrowing
+    edge[2, 64:] = np.linspace(-127, 127, 32) * 0.1                       # |q| up to 127
+    edge[3, :] = 0.0                                                      # all-zero blocks
+    xs = np.concatenate([x, edge]).astype(np.float32)
+    q["x"] = xs
+    b4, b8 = quantize_q4_0(xs), quantize_q8_0(xs)
+    q["q4_0"] = np.frombuffer(b4, np.uint8)
+    q["q8_0"] = np.frombuffer(b8, np.uint8)
+    q["deq_q4_0"] = dequantize_q4_0(b4, xs.shape)
+    q["deq_q8_0"] = dequantize_q8_0(b8, xs.shape)
+
+    tiny = VitConfig(depth=2, hidden_size=64, num_heads=4, intermediate_size=128,
+                     patch_size=4, temporal_patch_size=2, in_channels=3,
+                     spatial_merge_size=2, out_hidden_size=32, layernorm_eps=1e-6,
+                     rope_theta=10000.0, image_size=32, act_dtype="fp16",
+                     weight_dtype="fp16")
+    z = np.load(os.path.join(ref_root, "hexlib", "tests", "data", "qwen35_vision_tiny.npz"))
+    g = build_vision_encoder(tiny)
+    feeds = loader.feeds_from_params(g, tiny, lambda n: z[f"param::{n}"])
+    feeds["image"] = z["image"]
+    feeds = {k: (np.asarray(v, np.float16).astype(np.float32)
+                 if g.tensor(k).dtype == "fp16" else np.asarray(v, np.float32))
+             for k, v in feeds.items()}
+    m = compile_model(g, budget=1 << 22)
+    assert not isinstance(m, Err), m
+    wb = build_whole_plan_batch(m, feeds)
+    q["plan_blob"] = np.frombuffer(wb.blob, np.uint8)
+    q["plan_payload"] = np.frombuffer(bytes(wb.payload), np.uint8)
+    out_name = g.outputs[0]
+    po = wb.placements[out_name]
+    q["plan_out"] = np.array([po.offset, po.nbytes], np.int64)
+    q["plan_out_shape"] = np.array(g.tensor(out_name).shape, np.int64)
+    quantized = sorted(n for n, p in wb.placements.items() if p.dtype == "q4_0")
+    q["plan_quantized"] = np.frombuffer(json.dumps(quantized).encode(), np.uint8)
+    deq = dict(feeds)
+    for n in quantized:
+        w = np.asarray(feeds[n], np.float32)
+        deq[n] = dequantize_q4_0(quantize_q4_0(w), w.shape).astype(np.float16).astype(np.float32)
+    rep = interpreter.run(m, deq)
+    assert not isinstance(rep, Err), rep
+    q["plan_expected"] = np.asarray(rep.outputs[out_name], np.float32)
+    np.savez_compressed(os.path.join(HERE, "quant.npz"), **q)
+    print("wrote quant.npz")
+
+
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    args = [a for a in sys.argv[1:] if not a.startswith("--")]
+    root = args[0] if args else "/root/reference"
+    if "--quant-only" not in sys.argv:
+        main(root)
+    make_quant(root)

@@ -74,16 +74,45 @@ def test_images_beyond_the_buffer_are_refused(plan256):
     assert rc == wire.STATUS["ERR_INVAL_PARAMS"] and r.n_ops == 0
 
 
-def test_a_reference_q4_0_blob_is_refused_at_its_first_matmul():
+def test_a_reference_q4_0_blob_validates_end_to_end():
     # build_whole_plan_batch of the tiny plan, by the reference: its
-    # matmul_epilogue weights are q4_0, which this backend has no kernel for.
+    # matmul_epilogue weights are q4_0 (the DSP spec's weight dtype), which
+    # the dispatcher serves by dequantizing to fp16 ahead of the GEMM.
     blob = bytes(np.load(os.path.join(GOLDEN, "wire.npz"))["tiny_whole_plan"])
     size = wire.BUF.unpack_from(blob, 40)[1]
     rc, r = check(blob, [size])
-    assert rc == wire.STATUS["ERR_REQUIRES"]
-    assert r.results[-1].kind == 5 and r.results[-1].status == wire.STATUS["ERR_REQUIRES"]
-    assert all(x.ok for x in r.results[:-1])     # patchify and cast before it are fine
-    assert [x.kind for x in r.results[:-1]] == [6, 2]
+    assert rc == 1 and r.ok
+    hdr = wire.HDR.unpack_from(blob, 0)
+    assert r.n_ops == hdr[5] and 5 in [x.kind for x in r.results]
+
+
+def _first_matmul_weight(blob: bytes) -> int:
+    """Byte offset of the TensorDesc of the first matmul_epilogue's weight."""
+    hdr = wire.HDR.unpack_from(blob, 0)
+    n_ops, off_tensors, off_ops = hdr[5], hdr[7], hdr[8]
+    for i in range(n_ops):
+        op = wire.OP.unpack_from(blob, off_ops + i * wire.OP.size)
+        if op[0] == 5:
+            src1 = op[2 + wire.MAX_PARAMS + 1]
+            return off_tensors + src1 * wire.TENSOR.size
+    raise AssertionError("no matmul_epilogue in the blob")
+
+
+def test_bad_quantized_weights_are_refused():
+    blob = bytes(np.load(os.path.join(GOLDEN, "wire.npz"))["tiny_whole_plan"])
+    size = wire.BUF.unpack_from(blob, 40)[1]
+    off = _first_matmul_weight(blob)
+    # fp32 is no weight dtype (its byte count made consistent): ERR_REQUIRES
+    t = wire.TENSOR.unpack_from(blob, off)
+    k, n = t[5], t[6]
+    assert t[1] + k * n * 4 <= size
+    bad = _mutate(_mutate(blob, off + 12, "<I", wire.DTYPE_ID["fp32"]), off + 8, "<I", k * n * 4)
+    rc, r = check(bad, [size])
+    assert rc == wire.STATUS["ERR_REQUIRES"] and r.results[-1].kind == 5
+    # a byte count that is not whole q4_0 blocks of the shape
+    nbytes = struct.unpack_from("<I", blob, off + 8)[0]
+    rc, r = check(_mutate(blob, off + 8, "<I", nbytes + 18), [size])
+    assert rc == wire.STATUS["ERR_INVAL_PARAMS"]
 
 
 def _mutate(blob: bytes, off: int, fmt: str, value) -> bytes:

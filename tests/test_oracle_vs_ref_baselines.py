@@ -110,3 +110,21 @@ def test_matmul():
     y = np.empty((Bn, M, N), np.float16)
     cref.call("matmul_fp16", a, b, y, Bn, M, K, N)
     assert_close_f16(y, o16("matmul", (a, b), {}), what="matmul")
+
+
+@pytest.mark.parametrize("M,K,N,act", [(256, 768, 768, 0), (64, 768, 3072, 1), (8, 96, 64, 2)])
+def test_quantized_matmul_epilogue(M, K, N, act):
+    """The reference's only matmul_epilogue kernel takes a q4_0 weight
+    (baseline.c:49-97); the oracle's dequantize-to-fp16 statement of it must
+    agree, on weights packed by this repository's own quantizer."""
+    from hexlib_b200 import quant
+    from oracle import quant as oq
+    a = r16((M, K), 40)
+    w = (np.random.default_rng(41).standard_normal((K, N)) * 0.05).astype(np.float32)
+    bias = (np.random.default_rng(42).standard_normal(N) * 0.02).astype(np.float32)
+    raw = np.frombuffer(quant.quantize_q4_0(w), np.uint8).copy()
+    got = np.zeros((M, N), np.float16)
+    cref.call("matmul_epilogue_fp16", a, raw, bias, got, M, K, N, act)
+    act_name = {0: "none", 1: "gelu_tanh", 2: "gelu_erf"}[act]
+    want = oq.matmul_epilogue_quant(a, raw.tobytes(), bias, K, N, "q4_0", act_name)
+    assert_close_f16(got, ops.store(want, "fp16").astype(np.float16), what=f"q4_0 {act_name}")
