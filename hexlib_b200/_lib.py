@@ -68,6 +68,8 @@ _PROTOS: dict[str, list] = {
                                          c_vp],
     "hexlib_b200_matmul_epilogue_q8_0": [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp, c_u64,
                                          c_vp],
+    "hexlib_b200_matmul_epilogue_q4_0_noalloc": [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int,
+                                                 c_int, c_vp],
     "hexlib_b200_dequant_q4_0_fp16": [c_vp, c_vp, c_int, c_int, c_vp],
     "hexlib_b200_dequant_q8_0_fp16": [c_vp, c_vp, c_int, c_int, c_vp],
     "hexlib_b200_matmul_epilogue_residual_fp16": [c_vp, c_vp, c_vp, c_vp, c_vp,

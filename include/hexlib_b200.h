@@ -261,6 +261,17 @@ HEXLIB_B200_API int hexlib_b200_matmul_epilogue_q8_0(const void *a, const void *
                                                      const float *bias, void *out, int M,
                                                      int K, int N, int act, void *workspace,
                                                      uint64_t workspace_bytes, void *stream);
+/* The q4_0 matmul_epilogue above without a workspace argument and without
+ * allocating: its scratch is a fixed 8 MiB device array of the library, so
+ * K * N <= 4 Mi (ERR_VTCM_TOO_SMALL otherwise). No counterpart in the
+ * reference, whose kernels always receive a scratch from their caller. Calls
+ * that overlap in time share that scratch and race; issue them in order (one
+ * stream). The first call on a device looks the array up with that device
+ * current; make it before any stream capture begins. */
+HEXLIB_B200_API int hexlib_b200_matmul_epilogue_q4_0_noalloc(const void *a, const void *w,
+                                                             const float *bias, void *out,
+                                                             int M, int K, int N, int act,
+                                                             void *stream);
 /* q4_0 / q8_0 [K, N] -> fp16 [K, N] with the rounding above (w 2-byte
  * aligned, out 16-byte aligned): the dequantization step alone. */
 HEXLIB_B200_API int hexlib_b200_dequant_q4_0_fp16(const void *w, void *out, int K, int N,
