@@ -392,11 +392,14 @@ def run_b200(args) -> None:
     else:
         achieved = dwork / mean_s / 1e9
         peak, punit = pk["hbm"], "GB/s"
-    traffic = None
+    traffic, traffic_note = None, "no ncu capture of this kernel on record"
     try:
         with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
             tr = json.load(f)
-        traffic = tr.get(dname)
+        ent = tr.get(dname)
+        if ent is not None:
+            traffic = float(ent["bytes_per_launch"])
+            traffic_note = ent.get("source", "")
     except Exception:  # noqa: BLE001
         pass
 
@@ -439,7 +442,8 @@ def run_b200(args) -> None:
                          "peak": peak, "unit": punit, "frac": achieved / peak,
                          "peak_source": f"{pk['src']} "
                                         f"({'sustained bf16' if dbound == 'tensor' else 'hbm copy'})",
-                         "traffic": traffic, "share": dom_ns / total_ns},
+                         "traffic": traffic, "traffic_unit": "bytes per launch (dram read + write)",
+                         "traffic_source": traffic_note, "share": dom_ns / total_ns},
             "kernels": kernels[:8],
             "clocks": clk,
             "cpu_baseline": cpu,
