@@ -5,9 +5,13 @@
 // and re-reads an [H, T, T] score and probability tensor per image and
 // layer. Here the scores live only in tensor memory and registers.
 //
-// TENSOR-CORE PATH (D = 64). One CTA owns 256 queries of one head as two
-// 128-row tiles (a and b) and streams the keys in blocks of 128:
-//   warp 0     TMA: both Q tiles once, then K and V blocks into a 3-stage ring;
+// TENSOR-CORE PATH (D = 64). A persistent kernel, one CTA per SM, walking work
+// items of 256 queries of one head (two 128-row tiles, a and b) and streaming
+// each item's keys in blocks of 128; the next item's Q and keys load while the
+// current one finishes, and its first S products run during the current
+// item's epilogue:
+//   warp 0     TMA: each item's two Q tiles into one of two Q buffers, then
+//              its K and V blocks into a 3-stage ring;
 //   warp 1     one lane issues tcgen05.mma: S_t = Q_t K^T (M=128, N=128,
 //              K=64) into TMEM, and after the softmax has written P_t to
 //              TMEM, O_t = P_t V (M=128, N=64, K=128) with A read from TMEM;
@@ -45,7 +49,7 @@ constexpr int AT_D = 64;
 constexpr int AT_STAGES = 3;
 constexpr int AT_THREADS = 320;
 constexpr int AT_TILE = AT_BM * AT_D * 2;        // 16 KiB: one Q, K or V tile
-constexpr int AT_SMEM = 2 * AT_TILE + AT_STAGES * 2 * AT_TILE + 1024 + 256;
+constexpr int AT_SMEM = 4 * AT_TILE + AT_STAGES * 2 * AT_TILE + 1024 + 256;
 constexpr uint32_t AT_TMEM_COLS = 512;           // S_a, S_b: 128; O_a, O_b, P_a, P_b: 64
 
 struct AttnParams {
@@ -82,29 +86,31 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;                                  // [2][16 KiB]
-  uint8_t* sK = sQ + 2 * AT_TILE;                      // [STAGES][16 KiB]
+  uint8_t* sQ = smem;                                  // [2 buffers][2 tiles][16 KiB]
+  uint8_t* sK = sQ + 4 * AT_TILE;                      // [STAGES][16 KiB]
   uint8_t* sV = sK + AT_STAGES * AT_TILE;              // [STAGES][16 KiB]
-  uint64_t* q_full = reinterpret_cast<uint64_t*>(sV + AT_STAGES * AT_TILE);
-  uint64_t* kv_full = q_full + 1;
-  uint64_t* kv_empty = kv_full + AT_STAGES;
-  uint64_t* s_full = kv_empty + AT_STAGES;   // [2]
+  uint64_t* q_full = reinterpret_cast<uint64_t*>(sV + AT_STAGES * AT_TILE);   // [2]
+  uint64_t* q_empty = q_full + 2;            // [2]
+  uint64_t* kv_full = q_empty + 2;           // [STAGES]
+  uint64_t* kv_empty = kv_full + AT_STAGES;  // [STAGES]
+  uint64_t* s_full = kv_empty + AT_STAGES;   // [2 tiles]
   uint64_t* s_free = s_full + 2;             // [2]
   uint64_t* p_full = s_free + 2;             // [2]
   uint64_t* o_full = p_full + 2;             // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 2);
+  uint64_t* o_free = o_full + 2;             // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_free + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int64_t bh = blockIdx.x / p.q_pairs;
-  const int bimg = (int)(bh / p.H);
-  const int head = (int)(bh % p.H);
-  const int q0 = (int)(blockIdx.x % p.q_pairs) * (2 * AT_BM);
   const int nkv = (p.T + AT_BN - 1) / AT_BN;
+  const int64_t items = p.Bn * p.q_pairs;
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&q_full[b], 1);
+      mbar_init(&q_empty[b], 1);
+    }
     for (int s = 0; s < AT_STAGES; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
@@ -114,6 +120,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       mbar_init(&s_free[t], 4);
       mbar_init(&p_full[t], 4);
       mbar_init(&o_full[t], 1);
+      mbar_init(&o_free[t], 4);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -132,66 +139,93 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // Work item w (this CTA takes w = blockIdx.x, + gridDim.x, ...): the
+  // query pair w % q_pairs of head (w / q_pairs) % H of image w / q_pairs / H.
+  // Every barrier phase runs on across items: the i-th item of this CTA uses
+  // Q buffer i & 1 and key blocks g = i*nkv .. i*nkv + nkv - 1 of the CTA's
+  // stream.
   if (warp == 0) {
     if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, 2 * AT_TILE);
-      tma_load_3d(&tmQ, q_full, sQ, p.xq + head * AT_D, q0, bimg);
-      tma_load_3d(&tmQ, q_full, sQ + AT_TILE, p.xq + head * AT_D, q0 + AT_BM, bimg);
-      for (int j = 0; j < nkv; ++j) {
-        const int st = j % AT_STAGES;
-        const uint32_t ph = (uint32_t)(j / AT_STAGES) & 1u;
-        if (!mbar_wait(&kv_empty[st], ph ^ 1u, abort_flag, p.err)) goto done;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * AT_TILE);
-        tma_load_3d(&tmK, &kv_full[st], sK + st * AT_TILE, p.xk + head * AT_D, j * AT_BN, bimg);
-        tma_load_3d(&tmV, &kv_full[st], sV + st * AT_TILE, p.xv + head * AT_D, j * AT_BN, bimg);
+      uint32_t g = 0;
+      int64_t i = 0;
+      for (int64_t w = blockIdx.x; w < items; w += gridDim.x, ++i) {
+        const int64_t bh = w / p.q_pairs;
+        const int bimg = (int)(bh / p.H), head = (int)(bh % p.H);
+        const int q0 = (int)(w % p.q_pairs) * (2 * AT_BM);
+        const int qb = (int)(i & 1);
+        // the buffer's previous item (i - 2) has finished its S products
+        if (!mbar_wait(&q_empty[qb], ((uint32_t)(i >> 1) & 1u) ^ 1u, abort_flag, p.err))
+          goto done;
+        mbar_arrive_expect_tx(&q_full[qb], 2 * AT_TILE);
+        uint8_t* qdst = sQ + qb * 2 * AT_TILE;
+        tma_load_3d(&tmQ, &q_full[qb], qdst, p.xq + head * AT_D, q0, bimg);
+        tma_load_3d(&tmQ, &q_full[qb], qdst + AT_TILE, p.xq + head * AT_D, q0 + AT_BM, bimg);
+        for (int j = 0; j < nkv; ++j, ++g) {
+          const int st = (int)(g % AT_STAGES);
+          const uint32_t ph = (g / AT_STAGES) & 1u;
+          if (!mbar_wait(&kv_empty[st], ph ^ 1u, abort_flag, p.err)) goto done;
+          mbar_arrive_expect_tx(&kv_full[st], 2 * AT_TILE);
+          tma_load_3d(&tmK, &kv_full[st], sK + st * AT_TILE, p.xk + head * AT_D, j * AT_BN, bimg);
+          tma_load_3d(&tmV, &kv_full[st], sV + st * AT_TILE, p.xv + head * AT_D, j * AT_BN, bimg);
+        }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_f16_f32(AT_BM, AT_BN, false, false);
       constexpr uint32_t idesc_o = idesc_f16_f32(AT_BM, AT_D, false, true);
-      if (!mbar_wait(q_full, 0, abort_flag, p.err)) goto done;
-      // S_t(j) = Q_t K_j^T, once the softmax has read S_t(j-1) out of TMEM
-      auto issue_s = [&](int t, int j) -> bool {
-        const int st = j % AT_STAGES;
-        if (!mbar_wait(&kv_full[st], (uint32_t)(j / AT_STAGES) & 1u, abort_flag, p.err))
-          return false;
-        if (j > 0 && !mbar_wait(&s_free[t], (uint32_t)(j - 1) & 1u, abort_flag, p.err))
-          return false;
-        tc_fence_after();
-        const uint32_t qa = smem_u32(sQ + t * AT_TILE);
-        const uint32_t kb = smem_u32(sK + st * AT_TILE);
+      uint32_t g0 = 0;          // the item's first key block in the CTA's stream
+      int64_t i = 0;
+      for (int64_t w = blockIdx.x; w < items; w += gridDim.x, ++i, g0 += nkv) {
+        const int qb = (int)(i & 1);
+        if (!mbar_wait(&q_full[qb], (uint32_t)(i >> 1) & 1u, abort_flag, p.err)) goto done;
+        // S_t(j) = Q_t K_j^T, once the softmax has read S_t(j-1) out of TMEM
+        auto issue_s = [&](int t, int j) -> bool {
+          const uint32_t g = g0 + (uint32_t)j;
+          const int st = (int)(g % AT_STAGES);
+          if (!mbar_wait(&kv_full[st], (g / AT_STAGES) & 1u, abort_flag, p.err)) return false;
+          if (g > 0 && !mbar_wait(&s_free[t], (g - 1) & 1u, abort_flag, p.err)) return false;
+          tc_fence_after();
+          const uint32_t qa = smem_u32(sQ + (qb * 2 + t) * AT_TILE);
+          const uint32_t kb = smem_u32(sK + st * AT_TILE);
 #pragma unroll
-        for (int kk = 0; kk < AT_D / 16; ++kk)
-          umma_f16(tmem + (uint32_t)(t * AT_BN), sdesc_sw128(qa + kk * 32, 16, 1024),
-                   sdesc_sw128(kb + kk * 32, 16, 1024), idesc_s, kk ? 1u : 0u);
-        umma_commit(&s_full[t]);
-        return true;
-      };
-      // O_t += P_t(j) V_j (overwrite at j = 0); O_t stays in TMEM throughout
-      auto issue_pv = [&](int t, int j) -> bool {
-        const int st = j % AT_STAGES;
-        if (!mbar_wait(&p_full[t], (uint32_t)j & 1u, abort_flag, p.err)) return false;
-        tc_fence_after();
-        const uint32_t pa = tmem + 384u + (uint32_t)(t * 64);   // 16 keys = 8 columns
-        const uint32_t vb = smem_u32(sV + st * AT_TILE);
+          for (int kk = 0; kk < AT_D / 16; ++kk)
+            umma_f16(tmem + (uint32_t)(t * AT_BN), sdesc_sw128(qa + kk * 32, 16, 1024),
+                     sdesc_sw128(kb + kk * 32, 16, 1024), idesc_s, kk ? 1u : 0u);
+          umma_commit(&s_full[t]);
+          return true;
+        };
+        // O_t += P_t(j) V_j, overwriting at the item's first block -- once
+        // the previous item's epilogue has read O_t out of TMEM
+        auto issue_pv = [&](int t, int j) -> bool {
+          const uint32_t g = g0 + (uint32_t)j;
+          const int st = (int)(g % AT_STAGES);
+          if (!mbar_wait(&p_full[t], g & 1u, abort_flag, p.err)) return false;
+          if (j == 0 && i > 0 &&
+              !mbar_wait(&o_free[t], (uint32_t)((i - 1) & 1), abort_flag, p.err))
+            return false;
+          tc_fence_after();
+          const uint32_t pa = tmem + 384u + (uint32_t)(t * 64);   // 16 keys = 8 columns
+          const uint32_t vb = smem_u32(sV + st * AT_TILE);
 #pragma unroll
-        for (int kk = 0; kk < AT_BN / 16; ++kk)
-          umma_f16_ts(tmem + 256u + (uint32_t)(t * AT_D), pa + (uint32_t)(kk * 8),
-                      sdesc_sw128(vb + kk * 2048, 8192, 1024), idesc_o,
-                      (j > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&o_full[t]);
-        return true;
-      };
-      if (!issue_s(0, 0) || !issue_s(1, 0)) goto done;
-      for (int j = 0; j < nkv; ++j) {
-        // S(j+1) goes in ahead of P(j)V(j), so a tile's next scores are ready
-        // by the time its softmax finishes the current block.
-        if (j + 1 < nkv && !issue_s(0, j + 1)) goto done;
-        if (!issue_pv(0, j)) goto done;
-        if (j + 1 < nkv && !issue_s(1, j + 1)) goto done;
-        if (!issue_pv(1, j)) goto done;
-        umma_commit(&kv_empty[j % AT_STAGES]);   // K_j and V_j fully consumed
+          for (int kk = 0; kk < AT_BN / 16; ++kk)
+            umma_f16_ts(tmem + 256u + (uint32_t)(t * AT_D), pa + (uint32_t)(kk * 8),
+                        sdesc_sw128(vb + kk * 2048, 8192, 1024), idesc_o,
+                        (j > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&o_full[t]);
+          return true;
+        };
+        if (!issue_s(0, 0) || !issue_s(1, 0)) goto done;
+        for (int j = 0; j < nkv; ++j) {
+          // S(j+1) goes in ahead of P(j)V(j), so a tile's next scores are
+          // ready by the time its softmax finishes the current block.
+          if (j + 1 < nkv && !issue_s(0, j + 1)) goto done;
+          if (!issue_pv(0, j)) goto done;
+          if (j + 1 < nkv && !issue_s(1, j + 1)) goto done;
+          if (!issue_pv(1, j)) goto done;
+          umma_commit(&kv_empty[(g0 + (uint32_t)j) % AT_STAGES]);   // K_j, V_j consumed
+        }
+        umma_commit(&q_empty[qb]);          // every S of this item has read its Q
       }
     }
   } else {
@@ -210,114 +244,124 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     const uint32_t p_col = tmem + lane_off + 384u + (uint32_t)(t * 64);
     const float c = p.c_log2;
     constexpr float kRescale = 8.0f;
-    float m_run = -INFINITY, l_run = 0.f;
-
-    for (int j = 0; j < nkv; ++j) {
-      const bool ok = mbar_wait(&s_full[t], (uint32_t)j & 1u, abort_flag, p.err);
-      if (!__all_sync(0xffffffffu, ok)) goto done;
-      tc_fence_after();
-      uint32_t sv[AT_BN];
-#pragma unroll
-      for (int cc = 0; cc < AT_BN / 32; ++cc)
-        tmem_ld_32x32b_x32(s_col + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[cc * 32]));
-      tmem_ld_wait();
-      // S is in registers: hand its TMEM back for S(j+1)
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[t]);
-
-      const int valid = p.T - j * AT_BN;             // keys of this block that exist
-      if (valid < AT_BN) {
-#pragma unroll
-        for (int i = 0; i < AT_BN; ++i)
-          if (i >= valid) sv[i] = __float_as_uint(-INFINITY);
-      }
-      // row max: four chains of three-input maxima
-      float pm[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) pm[i] = __uint_as_float(sv[i]);
-#pragma unroll
-      for (int i = 4; i < AT_BN; i += 8)
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          pm[q] = max3f(pm[q], __uint_as_float(sv[i + q]), __uint_as_float(sv[i + 4 + q]));
-      // the scale is positive, so max(s)*c is the max of s*c
-      const float mx = c * max3f(pm[0], pm[1], fmaxf(pm[2], pm[3]));
-      const bool rescale = mx > m_run + kRescale;
-      const float m_use = rescale ? mx : m_run;
-      const float alpha = rescale ? ex2_approx(m_run - mx) : 1.0f;
-      // P V of the previous block must be done: it reads the P buffer this
-      // block overwrites, and a rescale (below) must see its contribution in O.
-      if (j > 0) {
-        const bool ok2 = mbar_wait(&o_full[t], (uint32_t)(j - 1) & 1u, abort_flag, p.err);
-        if (!__all_sync(0xffffffffu, ok2)) goto done;
+    uint32_t g0 = 0;
+    int64_t i = 0;
+    for (int64_t w = blockIdx.x; w < items; w += gridDim.x, ++i, g0 += nkv) {
+      const int64_t bh = w / p.q_pairs;
+      const int bimg = (int)(bh / p.H), head = (int)(bh % p.H);
+      const int q0 = (int)(w % p.q_pairs) * (2 * AT_BM);
+      float m_run = -INFINITY, l_run = 0.f;
+      for (int j = 0; j < nkv; ++j) {
+        const uint32_t g = g0 + (uint32_t)j;
+        const bool ok = mbar_wait(&s_full[t], g & 1u, abort_flag, p.err);
+        if (!__all_sync(0xffffffffu, ok)) goto done;
         tc_fence_after();
-      }
-      // p = 2^(s*c - m), 32 keys at a time: one FMA and one MUFU exponential
-      // per key, eight partial row sums, and the fp16 pairs stored to this
-      // row's lane of P in TMEM (column i holds keys 2i and 2i + 1).
-      float ps[8];
+        uint32_t sv[AT_BN];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) ps[i] = 0.f;
+        for (int cc = 0; cc < AT_BN / 32; ++cc)
+          tmem_ld_32x32b_x32(s_col + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[cc * 32]));
+        tmem_ld_wait();
+        // S is in registers: hand its TMEM back for S(j+1)
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[t]);
+
+        const int valid = p.T - j * AT_BN;             // keys of this block that exist
+        if (valid < AT_BN) {
 #pragma unroll
-      for (int k32 = 0; k32 < AT_BN / 32; ++k32) {
-        uint32_t h2[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int e = k32 * 32 + 2 * i;
-          const float p0 = ex2_approx(fmaf(__uint_as_float(sv[e]), c, -m_use));
-          const float p1 = ex2_approx(fmaf(__uint_as_float(sv[e + 1]), c, -m_use));
-          ps[(2 * i) & 7] += p0;
-          ps[(2 * i + 1) & 7] += p1;
-          h2[i] = pack_half2(p0, p1);
+          for (int e = 0; e < AT_BN; ++e)
+            if (e >= valid) sv[e] = __float_as_uint(-INFINITY);
         }
-        tmem_st_32x32b_x16(p_col + (uint32_t)(k32 * 16), h2);
-      }
-      const float rs = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
-      // O *= alpha before P V of this block is issued (rare: the max grew by
-      // more than 2^8 since the last rescale)
-      if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+        // row max: four chains of three-input maxima
+        float pm[4];
 #pragma unroll
-        for (int h = 0; h < AT_D / 32; ++h) {
-          uint32_t rg[32];
-          tmem_ld_32x32b_x32(o_col + h * 32, rg);
-          tmem_ld_wait();
+        for (int e = 0; e < 4; ++e) pm[e] = __uint_as_float(sv[e]);
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            rg[i] = __float_as_uint(__uint_as_float(rg[i]) * alpha);
-          tmem_st_32x32b_x32(o_col + h * 32, rg);
+        for (int e = 4; e < AT_BN; e += 8)
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            pm[q] = max3f(pm[q], __uint_as_float(sv[e + q]), __uint_as_float(sv[e + 4 + q]));
+        // the scale is positive, so max(s)*c is the max of s*c
+        const float mx = c * max3f(pm[0], pm[1], fmaxf(pm[2], pm[3]));
+        const bool rescale = mx > m_run + kRescale;
+        const float m_use = rescale ? mx : m_run;
+        const float alpha = rescale ? ex2_approx(m_run - mx) : 1.0f;
+        // P V of the previous block must be done: it reads the P buffer this
+        // block overwrites, and a rescale (below) must see its contribution
+        // in O. (At an item's first block the previous item's epilogue has
+        // already waited for its last P V.)
+        if (j > 0) {
+          const bool ok2 = mbar_wait(&o_full[t], (g - 1) & 1u, abort_flag, p.err);
+          if (!__all_sync(0xffffffffu, ok2)) goto done;
+          tc_fence_after();
         }
-        tmem_st_wait();
+        // p = 2^(s*c - m), 32 keys at a time: one FMA and one MUFU exponential
+        // per key, eight partial row sums, and the fp16 pairs stored to this
+        // row's lane of P in TMEM (column e holds keys 2e and 2e + 1).
+        float ps[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ps[e] = 0.f;
+#pragma unroll
+        for (int k32 = 0; k32 < AT_BN / 32; ++k32) {
+          uint32_t h2[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const int x = k32 * 32 + 2 * e;
+            const float p0 = ex2_approx(fmaf(__uint_as_float(sv[x]), c, -m_use));
+            const float p1 = ex2_approx(fmaf(__uint_as_float(sv[x + 1]), c, -m_use));
+            ps[(2 * e) & 7] += p0;
+            ps[(2 * e + 1) & 7] += p1;
+            h2[e] = pack_half2(p0, p1);
+          }
+          tmem_st_32x32b_x16(p_col + (uint32_t)(k32 * 16), h2);
+        }
+        const float rs = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+        // O *= alpha before P V of this block is issued (rare: the max grew by
+        // more than 2^8 since the last rescale)
+        if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+          for (int h = 0; h < AT_D / 32; ++h) {
+            uint32_t rg[32];
+            tmem_ld_32x32b_x32(o_col + h * 32, rg);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              rg[e] = __float_as_uint(__uint_as_float(rg[e]) * alpha);
+            tmem_st_32x32b_x32(o_col + h * 32, rg);
+          }
+          tmem_st_wait();
+        }
+        tmem_st_wait();                  // P (and a rescaled O) are in TMEM
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[t]);
+        l_run = l_run * alpha + rs;
+        m_run = m_use;
       }
-      tmem_st_wait();                  // P (and a rescaled O) are in TMEM
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[t]);
-      l_run = l_run * alpha + rs;
-      m_run = m_use;
-    }
-    {
-      const bool ok = mbar_wait(&o_full[t], (uint32_t)(nkv - 1) & 1u, abort_flag, p.err);
+      // the item's output: O out of TMEM (then its columns are free for the
+      // next item's first P V), divided by the row sum, rounded once
+      const bool ok = mbar_wait(&o_full[t], (g0 + (uint32_t)nkv - 1) & 1u, abort_flag, p.err);
       if (!__all_sync(0xffffffffu, ok)) goto done;
       tc_fence_after();
+      uint32_t ov[AT_D];
+      tmem_ld_32x32b_x32(o_col, *reinterpret_cast<uint32_t(*)[32]>(&ov[0]));
+      tmem_ld_32x32b_x32(o_col + 32, *reinterpret_cast<uint32_t(*)[32]>(&ov[32]));
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_free[t]);
       const int row = q0 + t * AT_BM + r;
-      const float inv = 1.0f / l_run;
-      uint4* dst = reinterpret_cast<uint4*>(
-          p.out + (((int64_t)bimg * p.T + row) * p.H + head) * (int64_t)AT_D);
+      if (row < p.T) {
+        const float inv = 1.0f / l_run;
+        uint4* dst = reinterpret_cast<uint4*>(
+            p.out + (((int64_t)bimg * p.T + row) * p.H + head) * (int64_t)AT_D);
 #pragma unroll
-      for (int h = 0; h < AT_D / 32; ++h) {
-        uint32_t rg[32];
-        tmem_ld_32x32b_x32(o_col + h * 32, rg);
-        tmem_ld_wait();
-        if (row < p.T) {
-#pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            const float* o = reinterpret_cast<const float*>(&rg[8 * g]);
-            dst[h * 4 + g] = make_uint4(pack_half2(o[0] * inv, o[1] * inv),
-                                        pack_half2(o[2] * inv, o[3] * inv),
-                                        pack_half2(o[4] * inv, o[5] * inv),
-                                        pack_half2(o[6] * inv, o[7] * inv));
-          }
+        for (int q = 0; q < AT_D / 8; ++q) {
+          const float* o = reinterpret_cast<const float*>(&ov[8 * q]);
+          dst[q] = make_uint4(pack_half2(o[0] * inv, o[1] * inv),
+                              pack_half2(o[2] * inv, o[3] * inv),
+                              pack_half2(o[4] * inv, o[5] * inv),
+                              pack_half2(o[6] * inv, o[7] * inv));
         }
       }
     }
@@ -389,6 +433,13 @@ int attention_kernels_init() {
   return HEXLIB_B200_OK;
 }
 
+// One CTA per SM (tensor memory holds one CTA's 512 columns), each looping
+// over work items; fewer CTAs when there are fewer items.
+unsigned persistent_grid(int64_t items) {
+  const int64_t sms = g_sms > 0 ? g_sms : 148;
+  return (unsigned)(items < sms ? items : sms);
+}
+
 int launch_attention(const void* q, const void* k, const void* v, void* ctx, int64_t Bn,
                      int T, int D, float scale, int* err, cudaStream_t s) {
   if (Bn < 0 || T <= 0 || D <= 0 || D > 256) return HEXLIB_B200_ERR_INVAL_PARAMS;
@@ -412,8 +463,7 @@ int launch_attention(const void* q, const void* k, const void* v, void* ctx, int
       p.c_log2 = scale * 1.4426950408889634f;
       p.out = reinterpret_cast<__half*>(ctx);
       p.err = err;
-      const int64_t grid = Bn * p.q_pairs;
-      attention_tc<<<(unsigned)grid, AT_THREADS, AT_SMEM, s>>>(mq, mk, mv, p);
+      attention_tc<<<persistent_grid(Bn * p.q_pairs), AT_THREADS, AT_SMEM, s>>>(mq, mk, mv, p);
       if (cudaPeekAtLastError() != cudaSuccess) {
         cudaGetLastError();
         return HEXLIB_B200_ERR_CUDA;
@@ -460,8 +510,7 @@ int launch_attention_qkv(const void* qkv, void* ctx, int64_t B, int T, int H, in
   p.c_log2 = scale * 1.4426950408889634f;
   p.out = reinterpret_cast<__half*>(ctx);
   p.err = err;
-  const int64_t grid = p.Bn * p.q_pairs;
-  attention_tc<<<(unsigned)grid, AT_THREADS, AT_SMEM, s>>>(m, m, m, p);
+  attention_tc<<<persistent_grid(p.Bn * p.q_pairs), AT_THREADS, AT_SMEM, s>>>(m, m, m, p);
   if (cudaPeekAtLastError() != cudaSuccess) {
     cudaGetLastError();
     return HEXLIB_B200_ERR_CUDA;

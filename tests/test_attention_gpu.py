@@ -50,6 +50,8 @@ def run_kernel(q, k, v, scale):
     (5, 300, 64, 1.0),
     (2, 64, 16, 1.0),        # tiny-config head dim: CUDA-core kernel
     (2, 130, 128, 1.0),      # wide heads: CUDA-core kernel
+    (160, 512, 64, 1.0),     # 320 work items: every CTA walks two or three
+    (300, 300, 64, 1.0),     # 600 items with ragged query and key tiles
 ])
 def test_attention_matches_exact_math(Bn, T, D, amp):
     rng = np.random.default_rng(Bn * 1000 + T)
