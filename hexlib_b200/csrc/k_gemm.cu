@@ -112,6 +112,24 @@ __device__ __forceinline__ void rope_head64(uint32_t (&lo)[16], uint32_t (&hi)[1
   }
 }
 
+// One whole 32-byte sector per thread (sm_100's 256-bit load): a residual
+// chunk row is two of these, so no half-used sector waits in L1 for its
+// other half. `p` 32-byte aligned.
+__device__ __forceinline__ void ld_nc_v8(const __half* p, uint4& lo, uint4& hi) {
+  asm volatile("ld.global.nc.v8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(lo.x), "=r"(lo.y), "=r"(lo.z), "=r"(lo.w), "=r"(hi.x), "=r"(hi.y),
+                 "=r"(hi.z), "=r"(hi.w)
+               : "l"(p));
+}
+// Read-only 16-byte load the L1 keeps in preference to streaming data.
+__device__ __forceinline__ float4 ld_nc_evict_last_f4(const float* p) {
+  float4 r;
+  asm volatile("ld.global.nc.L1::evict_last.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+               : "l"(p));
+  return r;
+}
+
 // One epilogue warp's share of a finished 128-row accumulator tile. TMEM
 // lanes [32*quarter, 32*quarter + 32) hold rows row0 + 32*quarter + lane of
 // batch entry b; the warp finishes the 64-column groups [g_lo, g_hi) of the
@@ -130,6 +148,28 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
   const __half* rrow =
       (p.resid && row_ok) ? p.resid + (b * p.M + row) * (int64_t)p.N : nullptr;
   const int rl = lane;                                        // row within the slab
+  // Residual chunks (32 columns = 64 B of this thread's row) are loaded one
+  // chunk ahead into a two-deep register buffer, as two whole 32-byte
+  // sectors when the residual is 32-byte aligned (row strides are: N % 8 == 0
+  // and 32-column chunks), else as four 16-byte loads.
+  uint4 res[2][4];
+  const bool res32 = (reinterpret_cast<uintptr_t>(p.resid) & 31u) == 0 && (p.N % 16) == 0;
+  auto load_res = [&](int g, int h, uint4 (&r)[4]) {
+    const int nc = n0 + g * 64 + h * 32;
+    if (res32) {
+#pragma unroll
+      for (int j = 0; j < 4; j += 2) {
+        if (nc + 8 * j < p.N) ld_nc_v8(rrow + nc + 8 * j, r[j], r[j + 1]);
+        else r[j] = r[j + 1] = make_uint4(0, 0, 0, 0);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        r[j] = (nc + 8 * j < p.N) ? __ldg(reinterpret_cast<const uint4*>(rrow + nc) + j)
+                                  : make_uint4(0, 0, 0, 0);
+    }
+  };
+  if (rrow && g_lo < g_hi) load_res(g_lo, 0, res[0]);
 #pragma unroll 1
   for (int g = g_lo; g < g_hi; ++g) {
     // the previous group's store must have finished reading the stage
@@ -139,27 +179,25 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int c32 = g * 64 + h * 32;          // column within the tile
-      const int nc = n0 + c32;             // global column
-      // issue the global loads first so their latency overlaps the TMEM read
+      const int nc = n0 + c32;                  // global column
+      // the next chunk's residual: (g, 1) after (g, 0); (g + 1, 0) after (g, 1)
+      if (rrow) {
+        if (h == 0) load_res(g, 1, res[1]);
+        else if (g + 1 < g_hi) load_res(g + 1, 0, res[0]);
+      }
       float bias[32];
       if (p.bias && nc < p.N) {
-        const float4* bp = reinterpret_cast<const float4*>(p.bias + nc);
+        const float* bp = p.bias + nc;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const float4 bb = (nc + 4 * j < p.N) ? __ldg(bp + j) : make_float4(0, 0, 0, 0);
+          const float4 bb = (nc + 4 * j < p.N) ? ld_nc_evict_last_f4(bp + 4 * j)
+                                               : make_float4(0, 0, 0, 0);
           bias[4 * j] = bb.x; bias[4 * j + 1] = bb.y;
           bias[4 * j + 2] = bb.z; bias[4 * j + 3] = bb.w;
         }
       } else {
 #pragma unroll
         for (int j = 0; j < 32; ++j) bias[j] = 0.f;
-      }
-      uint4 res[4];
-      if (rrow) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          res[j] = (nc + 8 * j < p.N) ? __ldg(reinterpret_cast<const uint4*>(rrow + nc) + j)
-                                      : make_uint4(0, 0, 0, 0);
       }
       uint32_t rg[32];
       tmem_ld_32x32b_x32(trow + c32, rg);
@@ -178,7 +216,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
       if (rrow) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const __half2* rh = reinterpret_cast<const __half2*>(&res[j]);
+          const __half2* rh = reinterpret_cast<const __half2*>(&res[h][j]);
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             // The matmul result is an fp16 tensor in the unfused plan:
