@@ -852,6 +852,37 @@ int gemm_kernels_init() {
   return HEXLIB_B200_OK;
 }
 
+// Tiling of a GEMM with N % 256 == 0 (no RoPE epilogue): CTA-pair 256x256
+// tiles or single-CTA 128x256 tiles, by the estimate `rounds x per-tile
+// cost` -- rounds of tiles over the CTAs that run at once (a tail round
+// costs a whole one), per-tile cost in units of one SM's share of a pair
+// tile. Fitted to measured encoder shapes at 8K-64K rows on B200: the pair's
+// lighter fill traffic pays where the mainloop bounds the tile (cost 1.0,
+// 1.03 for a single-CTA tile); with a GELU epilogue the epilogue bounds it
+// and the pair's cluster handshakes cost a little (1.05). 128x128 tiles
+// were slower at every measured shape and are used only when pinned:
+// HEXLIB_B200_GEMM_TILE = pair, 256 or 128 pins one (for measurements).
+enum { kTileAuto = 0, kTilePair = 1, kTile256 = 2, kTile128 = 3 };
+int g_tile_pin = -1;
+
+int choose_tiling(const GemmDesc& g) {
+  if (g_tile_pin < 0) {
+    const char* e = getenv("HEXLIB_B200_GEMM_TILE");
+    g_tile_pin = !e ? kTileAuto
+               : (e[0] == 'p' ? kTilePair : (e[0] == '2' ? kTile256 : (e[0] == '1' ? kTile128 : kTileAuto)));
+  }
+  const bool pair_ok = g_pair_clusters > 0 && g.b_shared && g.batch == 1;
+  if (g_tile_pin == kTilePair && pair_ok) return kTilePair;
+  if (g_tile_pin == kTile256) return kTile256;
+  if (g_tile_pin == kTile128) return kTile128;
+  if (!pair_ok) return kTile256;
+  auto rounds = [](int64_t tiles, int64_t slots) { return (tiles + slots - 1) / slots; };
+  const double c_pair = (double)rounds(((g.M + 255) / 256) * (g.N / 256), g_pair_clusters) *
+                        (g.act != 0 ? 1.05 : 1.0);
+  const double c_256 = (double)rounds(((g.M + 127) / 128) * (g.N / 256), sm_count()) * 1.03;
+  return c_pair <= c_256 ? kTilePair : kTile256;
+}
+
 int launch_gemm(const GemmDesc& g, int* err, cudaStream_t s) {
   if (g.batch < 0 || g.M < 0 || g.K <= 0 || g.N <= 0 || g.act < 0 ||
       g.act > 2 || !g.A || !g.B || !g.out)
@@ -868,8 +899,11 @@ int launch_gemm(const GemmDesc& g, int* err, cudaStream_t s) {
                       (!g.resid || aligned16(g.resid)) && tma_available();
   if (tma_ok) {
     int rc;
-    if (g.N % 256 == 0 && !rope && g_pair_clusters > 0)
+    const int tiling = (g.N % 256 == 0 && !rope) ? choose_tiling(g) : 0;
+    if (tiling == kTilePair)
       rc = launch_pair(g, err, s);
+    else if (tiling == kTile128)
+      rc = launch_tc<128, false>(g, err, s);
     else if (g.N % 256 == 0)
       rc = rope ? launch_tc<256, true>(g, err, s) : launch_tc<256, false>(g, err, s);
     else if (g.N % 128 == 0)
