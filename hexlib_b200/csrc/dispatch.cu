@@ -344,23 +344,26 @@ int check_op(const OpRec& op) {
       return HEXLIB_B200_OK;
     }
     case HEXLIB_B200_KIND_MATMUL_EPILOGUE_ROPE: {
-      HB_TRY(need(op, 6));
+      // a, w, bias, seg_cos [n, 16], seg_sin [n, 16], seg_idx [T, 2] int32, out
+      HB_TRY(need(op, 7));
       HB_TRY(dt(op, 0, DT_FP16));
       HB_TRY(dt(op, 1, DT_FP16));
       HB_TRY(dt(op, 2, DT_FP32));
       HB_TRY(dt(op, 3, DT_FP32));
       HB_TRY(dt(op, 4, DT_FP32));
-      HB_TRY(dt(op, 5, DT_FP16));
-      HB_TRY(batching(op, 5));
+      HB_TRY(dt(op, 5, DT_INT32));
+      HB_TRY(dt(op, 6, DT_FP16));
+      HB_TRY(batching(op, 6));
       const uint32_t* a = op.a[0].ne;   // M, K
       const uint32_t* w = op.a[1].ne;   // K, N
-      const uint32_t* c = op.a[3].ne;   // T, 64
+      const uint32_t* c = op.a[3].ne;   // n_seg, 16
+      const uint32_t* x = op.a[5].ne;   // T, 2
       if (a[2] != 1 || a[3] != 1 || w[2] != 1 || w[3] != 1 || w[0] != a[1] || a[1] == 0 ||
           w[1] == 0 || numel(op.a[2].ne) != w[1] || op.a[1].per_image ||
-          op.a[2].per_image || op.a[3].per_image || op.a[4].per_image ||
-          memcmp(op.a[3].ne, op.a[4].ne, sizeof(uint32_t) * 4) != 0 || c[1] != 64 ||
-          c[2] != 1 || c[3] != 1 || c[0] == 0 || a[0] % c[0] != 0 ||
-          numel(op.a[5].ne) != (uint64_t)a[0] * w[1])
+          op.a[2].per_image || op.a[3].per_image || op.a[4].per_image || op.a[5].per_image ||
+          memcmp(op.a[3].ne, op.a[4].ne, sizeof(uint32_t) * 4) != 0 || c[0] == 0 ||
+          c[1] != 16 || c[2] != 1 || c[3] != 1 || x[0] == 0 || x[1] != 2 || x[2] != 1 ||
+          x[3] != 1 || a[0] % x[0] != 0 || numel(op.a[6].ne) != (uint64_t)a[0] * w[1])
         return HEXLIB_B200_ERR_INVAL_PARAMS;
       if (op.params[0] < 0 || op.params[0] > 2 || op.params[1] <= 0 || op.params[1] % 64 ||
           (uint32_t)op.params[1] > w[1] || w[1] % 64)
@@ -519,7 +522,7 @@ int run_op(const OpRec& op, uint32_t n_images, int* err, void* ws, uint64_t ws_b
       g.A = a[0].ptr;
       g.B = a[1].ptr;
       g.bias = (const float*)a[2].ptr;
-      g.out = a[5].ptr;
+      g.out = a[6].ptr;
       g.batch = 1;
       g.M = (int64_t)a[0].ne[0] * B;
       g.K = (int)a[0].ne[1];
@@ -528,7 +531,9 @@ int run_op(const OpRec& op, uint32_t n_images, int* err, void* ws, uint64_t ws_b
       g.act = op.params[0];
       g.rope_cos = (const float*)a[3].ptr;
       g.rope_sin = (const float*)a[4].ptr;
-      g.rope_T = (int)a[3].ne[0];
+      g.rope_idx = (const int*)a[5].ptr;
+      g.rope_nseg = (int)a[3].ne[0];
+      g.rope_T = (int)a[5].ne[0];
       g.rope_cols = op.params[1];
       return hb::launch_gemm(g, err, s);
     }

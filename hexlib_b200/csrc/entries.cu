@@ -263,12 +263,13 @@ int hexlib_b200_matmul_epilogue_residual_fp16(const void* a, const void* w,
 }
 
 int hexlib_b200_matmul_epilogue_rope_fp16(const void* a, const void* w, const float* bias,
-                                          const float* costab, const float* sintab, void* out,
-                                          int M, int K, int N, int act, int rope_cols, int T,
+                                          const float* seg_cos, const float* seg_sin,
+                                          const int* seg_idx, int n_seg, void* out, int M,
+                                          int K, int N, int act, int rope_cols, int T,
                                           void* stream) {
   HB_ENTRY_INIT();
-  if (M < 0 || K <= 0 || N <= 0 || act < 0 || act > 2 || !bias || !costab || !sintab ||
-      rope_cols <= 0 || T <= 0 || (M % T) != 0)
+  if (M < 0 || K <= 0 || N <= 0 || act < 0 || act > 2 || !bias || !seg_cos || !seg_sin ||
+      !seg_idx || n_seg <= 0 || rope_cols <= 0 || T <= 0 || (M % T) != 0)
     return HEXLIB_B200_ERR_INVAL_PARAMS;
   hb::GemmDesc g{};
   g.A = a;
@@ -281,8 +282,10 @@ int hexlib_b200_matmul_epilogue_rope_fp16(const void* a, const void* w, const fl
   g.N = N;
   g.b_shared = true;
   g.act = act;
-  g.rope_cos = costab;
-  g.rope_sin = sintab;
+  g.rope_cos = seg_cos;
+  g.rope_sin = seg_sin;
+  g.rope_idx = seg_idx;
+  g.rope_nseg = n_seg;
   g.rope_T = T;
   g.rope_cols = rope_cols;
   return hb::launch_gemm(g, hb::default_error_word(), as_stream(stream));

@@ -70,10 +70,15 @@ struct GemmDesc {
   bool b_shared;       // B has one copy used by every batch entry
   int act;             // 0 none, 1 gelu_tanh, 2 gelu_erf
   // RoPE epilogue: when rope_cols > 0, columns [0, rope_cols) are 64-wide
-  // heads rotated with row r's token r % rope_T of the [rope_T, 64] tables,
-  // after the fp16 rounding of act(A@W + bias) (the rope_2d op on q/k).
+  // heads rotated for row r's token t = r % rope_T, after the fp16 rounding
+  // of act(A@W + bias) (the rope_2d op on q/k). The [rope_T, 64] cos/sin
+  // tables are half-symmetric (dims i and i + 32 share a value) and come as
+  // 16-wide segments: dims [16s, 16s + 16) and [32 + 16s, 48 + 16s) of token
+  // t are row rope_idx[2t + s] of the [n, 16] fp32 tables rope_cos / rope_sin.
   const float* rope_cos = nullptr;
   const float* rope_sin = nullptr;
+  const int* rope_idx = nullptr;   // [rope_T, 2]; entries clamped to [0, rope_nseg)
+  int rope_nseg = 0;
   int rope_T = 0;
   int rope_cols = 0;
 };

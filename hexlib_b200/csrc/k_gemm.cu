@@ -71,46 +71,16 @@ struct GemmParams {
   __half* out;
   int* err;
   // RoPE epilogue (ROPE kernels only): columns [0, rope_cols) are heads of
-  // 64; row r is token r % rope_T of the [rope_T, 64] cos/sin tables.
+  // 64; row r is token r % rope_T, whose dims [16s, 16s + 16) and
+  // [32 + 16s, 48 + 16s), s = 0, 1, take row rope_idx[2 * token + s] of the
+  // [n, 16] segment tables.
   const float* rope_cos;
   const float* rope_sin;
+  const int* rope_idx;
+  int rope_nseg;
   int rope_T;
   int rope_cols;
 };
-
-// Split-half rotation of one 64-column head (kernels/rope_2d_fp16/kernel_api.h:
-// 17-26) applied to fp16-rounded inputs with separately rounded products, as
-// the rope_2d op computes it on the stored q/k.
-__device__ __forceinline__ void rope_head64(uint32_t (&lo)[16], uint32_t (&hi)[16],
-                                            const float* __restrict__ ct,
-                                            const float* __restrict__ st) {
-#pragma unroll
-  for (int i = 0; i < 16; i += 4) {
-    const float4 c0 = __ldg(reinterpret_cast<const float4*>(ct + 2 * i));
-    const float4 c1 = __ldg(reinterpret_cast<const float4*>(ct + 2 * i + 4));
-    const float4 c2 = __ldg(reinterpret_cast<const float4*>(ct + 32 + 2 * i));
-    const float4 c3 = __ldg(reinterpret_cast<const float4*>(ct + 32 + 2 * i + 4));
-    const float4 s0 = __ldg(reinterpret_cast<const float4*>(st + 2 * i));
-    const float4 s1 = __ldg(reinterpret_cast<const float4*>(st + 2 * i + 4));
-    const float4 s2 = __ldg(reinterpret_cast<const float4*>(st + 32 + 2 * i));
-    const float4 s3 = __ldg(reinterpret_cast<const float4*>(st + 32 + 2 * i + 4));
-    const float cl[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-    const float ch[8] = {c2.x, c2.y, c2.z, c2.w, c3.x, c3.y, c3.z, c3.w};
-    const float sl[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-    const float sh[8] = {s2.x, s2.y, s2.z, s2.w, s3.x, s3.y, s3.z, s3.w};
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&lo[i + q]));
-      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&hi[i + q]));
-      const float y0 = __fadd_rn(__fmul_rn(a.x, cl[2 * q]), __fmul_rn(-b.x, sl[2 * q]));
-      const float y1 = __fadd_rn(__fmul_rn(a.y, cl[2 * q + 1]), __fmul_rn(-b.y, sl[2 * q + 1]));
-      const float z0 = __fadd_rn(__fmul_rn(b.x, ch[2 * q]), __fmul_rn(a.x, sh[2 * q]));
-      const float z1 = __fadd_rn(__fmul_rn(b.y, ch[2 * q + 1]), __fmul_rn(a.y, sh[2 * q + 1]));
-      lo[i + q] = pack_half2(y0, y1);
-      hi[i + q] = pack_half2(z0, z1);
-    }
-  }
-}
 
 // One whole 32-byte sector per thread (sm_100's 256-bit load): a residual
 // chunk row is two of these, so no half-used sector waits in L1 for its
@@ -130,6 +100,53 @@ __device__ __forceinline__ float4 ld_nc_evict_last_f4(const float* p) {
   return r;
 }
 
+// Split-half rotation of one 64-column head (kernels/rope_2d_fp16/kernel_api.h:
+// 17-26) applied to fp16-rounded inputs with separately rounded products, as
+// the rope_2d op computes it on the stored q/k. lo holds dims 0..31, hi dims
+// 32..63 (two per 32-bit word). The tables are half-symmetric (cos[i] ==
+// cos[i + 32], as every rotate-half table built from one frequency list is),
+// so rc / rs hold the cos / sin of dims 0..31, which dims 32..63 reuse.
+__device__ __forceinline__ void rope_head64(uint32_t (&lo)[16], uint32_t (&hi)[16],
+                                            const float (&rc)[32], const float (&rs)[32]) {
+#pragma unroll
+  for (int q = 0; q < 16; ++q) {
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&lo[q]));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&hi[q]));
+    const float c0 = rc[2 * q], c1 = rc[2 * q + 1], s0 = rs[2 * q], s1 = rs[2 * q + 1];
+    const float y0 = __fadd_rn(__fmul_rn(a.x, c0), __fmul_rn(-b.x, s0));
+    const float y1 = __fadd_rn(__fmul_rn(a.y, c1), __fmul_rn(-b.y, s1));
+    const float z0 = __fadd_rn(__fmul_rn(b.x, c0), __fmul_rn(a.x, s0));
+    const float z1 = __fadd_rn(__fmul_rn(b.y, c1), __fmul_rn(a.y, s1));
+    lo[q] = pack_half2(y0, y1);
+    hi[q] = pack_half2(z0, z1);
+  }
+}
+
+// The cos / sin of dims 0..31 of token `tok` from the segment tables: two
+// 16-float rows each, a few KiB for a whole image, so they stay in L1 while
+// every row of every tile reads them.
+__device__ __forceinline__ void rope_row(const GemmParams& p, int64_t tok, float (&rc)[32],
+                                         float (&rs)[32]) {
+  int2 ix = __ldg(reinterpret_cast<const int2*>(p.rope_idx) + tok);
+  const int top = p.rope_nseg - 1;                // never read outside the tables
+  ix.x = min(max(ix.x, 0), top);
+  ix.y = min(max(ix.y, 0), top);
+#pragma unroll
+  for (int s = 0; s < 2; ++s) {
+    const float* cp = p.rope_cos + (s ? ix.y : ix.x) * 16;
+    const float* sp = p.rope_sin + (s ? ix.y : ix.x) * 16;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float4 c = ld_nc_evict_last_f4(cp + 4 * j);
+      const float4 n = ld_nc_evict_last_f4(sp + 4 * j);
+      rc[16 * s + 4 * j] = c.x; rc[16 * s + 4 * j + 1] = c.y;
+      rc[16 * s + 4 * j + 2] = c.z; rc[16 * s + 4 * j + 3] = c.w;
+      rs[16 * s + 4 * j] = n.x; rs[16 * s + 4 * j + 1] = n.y;
+      rs[16 * s + 4 * j + 2] = n.z; rs[16 * s + 4 * j + 3] = n.w;
+    }
+  }
+}
+
 // One epilogue warp's share of a finished 128-row accumulator tile. TMEM
 // lanes [32*quarter, 32*quarter + 32) hold rows row0 + 32*quarter + lane of
 // batch entry b; the warp finishes the 64-column groups [g_lo, g_hi) of the
@@ -145,8 +162,15 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
   const int64_t row = row0 + quarter * 32 + lane;
   const bool row_ok = row < p.M;
   const uint32_t trow = tacc + ((uint32_t)(quarter * 32) << 16);
+  // (the RoPE kernels take no residual)
   const __half* rrow =
-      (p.resid && row_ok) ? p.resid + (b * p.M + row) * (int64_t)p.N : nullptr;
+      (!ROPE && p.resid && row_ok) ? p.resid + (b * p.M + row) * (int64_t)p.N : nullptr;
+  // the row's cos / sin, loaded once for every head of the tile
+  float rc[32], rs[32];
+  const bool rope_row_ok = ROPE && row_ok && n0 + g_lo * 64 < p.rope_cols;
+  if constexpr (ROPE) {
+    if (rope_row_ok) rope_row(p, row % p.rope_T, rc, rs);
+  }
   const int rl = lane;                                        // row within the slab
   // Residual chunks (32 columns = 64 B of this thread's row) are loaded one
   // chunk ahead into a two-deep register buffer, as two whole 32-byte
@@ -234,13 +258,8 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
 #pragma unroll
       for (int q = 0; q < 16; ++q) packed[h][q] = hw[q];
     }
-    if (ROPE) {
-      const int n64 = n0 + g * 64;
-      if (n64 < p.rope_cols && row_ok) {
-        const int tok = (int)(row % p.rope_T);
-        rope_head64(packed[0], packed[1], p.rope_cos + (int64_t)tok * 64,
-                    p.rope_sin + (int64_t)tok * 64);
-      }
+    if constexpr (ROPE) {
+      if (rope_row_ok && n0 + g * 64 < p.rope_cols) rope_head64(packed[0], packed[1], rc, rs);
     }
     // 8 x 16 B into the 128-byte row rl of the stage, swizzled
 #pragma unroll
@@ -449,6 +468,7 @@ struct PairCfg {
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGING + 1024 + 256;
 };
 
+template <bool ROPE>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_f16_pair(const __grid_constant__ CUtensorMap tmA,
                   const __grid_constant__ CUtensorMap tmB,
@@ -597,7 +617,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         goto done;
       }
       tc_fence_after();
-      epilogue_tile<false>(p, &tmC, tmem_base + (uint32_t)(acc * BN), stage, quarter, lane,
+      epilogue_tile<ROPE>(p, &tmC, tmem_base + (uint32_t)(acc * BN), stage, quarter, lane,
                            g_lo, g_hi, b, (int64_t)mb * (2 * BM) + rank * BM, nb * BN);
       tc_fence_before();
       __syncwarp();
@@ -725,6 +745,8 @@ int launch_tc(const GemmDesc& g, int* err, cudaStream_t s) {
   p.err = err;
   p.rope_cos = g.rope_cos;
   p.rope_sin = g.rope_sin;
+  p.rope_idx = g.rope_idx;
+  p.rope_nseg = g.rope_nseg;
   p.rope_T = g.rope_T > 0 ? g.rope_T : 1;
   p.rope_cols = ROPE ? g.rope_cols : 0;
   const int64_t grid64 =
@@ -746,6 +768,7 @@ bool aligned16(const void* p) {
 // found once by the occupancy calculator for clusters of two.
 int g_pair_clusters = 0;
 
+template <bool ROPE>
 int launch_pair(const GemmDesc& g, int* err, cudaStream_t s) {
   using Cfg = PairCfg;
   CUtensorMap ta, tb, tcm;
@@ -773,10 +796,12 @@ int launch_pair(const GemmDesc& g, int* err, cudaStream_t s) {
   p.resid = reinterpret_cast<const __half*>(g.resid);
   p.out = reinterpret_cast<__half*>(g.out);
   p.err = err;
-  p.rope_cos = nullptr;
-  p.rope_sin = nullptr;
-  p.rope_T = 1;
-  p.rope_cols = 0;
+  p.rope_cos = g.rope_cos;
+  p.rope_sin = g.rope_sin;
+  p.rope_idx = g.rope_idx;
+  p.rope_nseg = g.rope_nseg;
+  p.rope_T = g.rope_T > 0 ? g.rope_T : 1;
+  p.rope_cols = ROPE ? g.rope_cols : 0;
   const int64_t pairs =
       p.total_tiles < g_pair_clusters ? p.total_tiles : (int64_t)g_pair_clusters;
   cudaLaunchConfig_t cfg = {};
@@ -791,7 +816,7 @@ int launch_pair(const GemmDesc& g, int* err, cudaStream_t s) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, gemm_f16_pair, ta, tb, tcm, p) != cudaSuccess) {
+  if (cudaLaunchKernelEx(&cfg, gemm_f16_pair<ROPE>, ta, tb, tcm, p) != cudaSuccess) {
     cudaGetLastError();
     return HEXLIB_B200_ERR_CUDA;
   }
@@ -826,7 +851,9 @@ int gemm_kernels_init() {
   g_pair_clusters = 0;
   const char* env = getenv("HEXLIB_B200_GEMM_PAIR");
   if (!(env && env[0] == '0') &&
-      cudaFuncSetAttribute(gemm_f16_pair, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      cudaFuncSetAttribute(gemm_f16_pair<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           PairCfg::SMEM_BYTES) == cudaSuccess &&
+      cudaFuncSetAttribute(gemm_f16_pair<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            PairCfg::SMEM_BYTES) == cudaSuccess) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (unsigned)sm_count(), 1, 1);
@@ -840,7 +867,7 @@ int gemm_kernels_init() {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, gemm_f16_pair, &cfg) == cudaSuccess && n > 0)
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_f16_pair<false>, &cfg) == cudaSuccess && n > 0)
       g_pair_clusters = n;
     cudaGetLastError();
   }
@@ -852,7 +879,7 @@ int gemm_kernels_init() {
   return HEXLIB_B200_OK;
 }
 
-// Tiling of a GEMM with N % 256 == 0 (no RoPE epilogue): CTA-pair 256x256
+// Tiling of a GEMM with N % 256 == 0: CTA-pair 256x256
 // tiles or single-CTA 128x256 tiles, by the estimate `rounds x per-tile
 // cost` -- rounds of tiles over the CTAs that run at once (a tail round
 // costs a whole one), per-tile cost in units of one SM's share of a pair
@@ -890,8 +917,9 @@ int launch_gemm(const GemmDesc& g, int* err, cudaStream_t s) {
   if (g.batch == 0 || g.M == 0) return HEXLIB_B200_OK;
   const bool rope = g.rope_cols > 0;
   if (rope && (g.rope_cols % 64 || g.rope_cols > g.N || g.N % 64 || g.rope_T <= 0 ||
-               !g.rope_cos || !g.rope_sin || !aligned16(g.rope_cos) ||
-               !aligned16(g.rope_sin)))
+               g.rope_nseg <= 0 || !g.rope_cos || !g.rope_sin || !g.rope_idx ||
+               !aligned16(g.rope_cos) ||
+               !aligned16(g.rope_sin) || !aligned16(g.rope_idx)))
     return HEXLIB_B200_ERR_INVAL_PARAMS;
   const bool tma_ok = (g.K % 8) == 0 && (g.N % 8) == 0 && aligned16(g.A) &&
                       aligned16(g.B) && aligned16(g.out) &&
@@ -899,9 +927,11 @@ int launch_gemm(const GemmDesc& g, int* err, cudaStream_t s) {
                       (!g.resid || aligned16(g.resid)) && tma_available();
   if (tma_ok) {
     int rc;
-    const int tiling = (g.N % 256 == 0 && !rope) ? choose_tiling(g) : 0;
+    const int tiling = (g.N % 256 == 0) ? choose_tiling(g) : 0;
     if (tiling == kTilePair)
-      rc = launch_pair(g, err, s);
+      rc = rope ? launch_pair<true>(g, err, s) : launch_pair<false>(g, err, s);
+    else if (tiling == kTile128 && rope)
+      rc = launch_tc<128, true>(g, err, s);
     else if (tiling == kTile128)
       rc = launch_tc<128, false>(g, err, s);
     else if (g.N % 256 == 0)

@@ -458,7 +458,7 @@ def fuse_residual(graph: Graph) -> Graph:
     return Graph(tensors, tuple(ops), graph.inputs, graph.outputs)
 
 
-def fuse_qkv(graph: Graph) -> tuple[Graph, dict[str, tuple]]:
+def fuse_qkv(graph: Graph, rope_epilogue: bool = False) -> tuple[Graph, dict[str, tuple]]:
     """CUDA-only, after `fuse_attention`: per block, the q, k and v projections
     (three matmul_epilogue over one input), their reshapes to [T, H, D], the
     rope_2d of q and k, the three [T,H,D] -> [H,T,D] transposes into the
@@ -468,10 +468,25 @@ def fuse_qkv(graph: Graph) -> tuple[Graph, dict[str, tuple]]:
         qkv   = rope_qk(raw, cos, sin)                       [T, 3, H, D]  (in place)
         ctx.t = attention_qkv(qkv)                           [T, H, D]
 
-    The concatenated weight and bias are new consts, returned as
-    `{name: ("concat", (parts...), axis)}` for the batch builder to derive from
-    the feeds. Every removed intermediate must have exactly one consumer and
-    not be a graph output; anything else leaves the block as it was."""
+    or, with `rope_epilogue` and an fp16 weight, the rotation applied by the
+    GEMM's epilogue before the one fp16 store:
+
+        qkv   = matmul_epilogue_rope(a, [wq|wk|wv], [bq|bk|bv],
+                                     seg_cos, seg_sin, seg_idx)  [T, 3, H, D]
+        ctx.t = attention_qkv(qkv)
+
+    where seg_cos / seg_sin [2T, 16] and seg_idx [T, 2] int32 are the
+    half-symmetric cos/sin tables cut into 16-wide segments and deduplicated
+    (a 2-D RoPE repeats each segment across a row or column of the patch
+    grid, so the distinct ones are few and stay cache-resident under the
+    epilogue); the batch builder refuses tables that are not half-symmetric.
+
+    The concatenated weight and bias and the segment tables are new consts,
+    returned as `{name: ("concat", (parts...), axis)}` and
+    `{name: ("rope_segments", (cos, sin), which)}` for the batch builder to
+    derive from the feeds. Every removed intermediate must have exactly one
+    consumer and not be a graph output; anything else leaves the block as it
+    was."""
     cons = _consumers(graph)
     protected = set(graph.outputs)
     producer = {o.outputs[0]: o for o in graph.ops}
@@ -546,10 +561,22 @@ def fuse_qkv(graph: Graph) -> tuple[Graph, dict[str, tuple]]:
         new_tensors[qkv] = Tensor(qkv, "fp16", (n_tok, 3, heads, d), False)
         derived[wname] = ("concat", tuple(ws), 1)
         derived[bname] = ("concat", tuple(bs), 0)
-        rewritten[mms[0].id] = Op(mms[0].id, "matmul_epilogue", (a, wname, bname), (raw,),
-                                  {"act": "none"})
-        # the rope takes the k projection's op id, free once that op is gone
-        rewritten[mms[1].id] = Op(mms[1].id, "rope_qk", (raw, cos, sin), (qkv,), {})
+        if rope_epilogue and wdt == "fp16":
+            segs = tuple(f"rope_segments({cos},{sin}).{w}" for w in ("cos", "sin", "idx"))
+            new_tensors[segs[0]] = Tensor(segs[0], "fp32", (2 * n_tok, 16), True)
+            new_tensors[segs[1]] = Tensor(segs[1], "fp32", (2 * n_tok, 16), True)
+            new_tensors[segs[2]] = Tensor(segs[2], "int32", (n_tok, 2), True)
+            for i, sname in enumerate(segs):
+                derived[sname] = ("rope_segments", (cos, sin), i)
+            del new_tensors[raw]
+            rewritten[mms[0].id] = Op(mms[0].id, "matmul_epilogue_rope",
+                                      (a, wname, bname) + segs, (qkv,),
+                                      {"act": "none", "rope_cols": 2 * heads * d})
+        else:
+            rewritten[mms[0].id] = Op(mms[0].id, "matmul_epilogue", (a, wname, bname), (raw,),
+                                      {"act": "none"})
+            # the rope takes the k projection's op id, free once that op is gone
+            rewritten[mms[1].id] = Op(mms[1].id, "rope_qk", (raw, cos, sin), (qkv,), {})
         rewritten[ctx_t.id] = Op(ctx_t.id, "attention_qkv", (qkv,), ctx_t.outputs,
                                  {"scale": float(att.attrs["scale"])})
         for w in "qkv":
@@ -561,7 +588,8 @@ def fuse_qkv(graph: Graph) -> tuple[Graph, dict[str, tuple]]:
         consumed.add(att.id)
         dropped.add(att.outputs[0])
         consumed.discard(mms[0].id)
-        consumed.discard(mms[1].id)
+        if mms[1].id in rewritten:
+            consumed.discard(mms[1].id)
     if not rewritten:
         return graph, {}
     ops = tuple(rewritten.get(o.id, o) for o in graph.ops
@@ -587,7 +615,8 @@ class ExecPlan:
     Shaped like the reference's `Compiled(graph, plan)` (compiled.py:33-66)
     where the batch builder reads it: `.graph` and `.plan.steps[i].op`.
     `derived` names consts a rewrite created, with the recipe that builds
-    each from the feeds (`("concat", parts, axis)`)."""
+    each from the feeds (`("concat", parts, axis)` or
+    `("rope_segments", (cos, sin), which)`)."""
     graph: Graph
     plan: "ExecSteps"
     derived: Mapping[str, tuple] = field(default_factory=dict)
@@ -599,12 +628,13 @@ class ExecSteps:
     target: str = "b200"
 
 
-def _apply_rewrites(g: Graph, attention: bool, residual: bool, qkv: bool):
+def _apply_rewrites(g: Graph, attention: bool, residual: bool, qkv: bool,
+                    rope_epilogue: bool = False):
     derived: dict[str, tuple] = {}
     if attention or qkv:
         g = fuse_attention(g)
     if qkv:
-        g, derived = fuse_qkv(g)
+        g, derived = fuse_qkv(g, rope_epilogue)
     if residual:
         g = fuse_residual(g)
     problems = g.problems()
@@ -614,26 +644,27 @@ def _apply_rewrites(g: Graph, attention: bool, residual: bool, qkv: bool):
 
 
 def compile_for_cuda(graph: Graph, attention: bool = False, residual: bool = False,
-                     qkv: bool = False) -> ExecPlan:
+                     qkv: bool = False, rope_epilogue: bool = False) -> ExecPlan:
     """Fuse (as the reference pipeline does), optionally apply the CUDA-only
     rewrites, and order the ops for execution (the builder's order is
-    topological; every rewrite keeps it so). `qkv` implies `attention`."""
+    topological; every rewrite keeps it so). `qkv` implies `attention`;
+    `rope_epilogue` moves the packed path's RoPE into the qkv GEMM."""
     problems = graph.problems()
     if problems:
         raise ValueError("graph is structurally invalid: " + "; ".join(problems[:5]))
-    g, derived = _apply_rewrites(fuse(graph), attention, residual, qkv)
+    g, derived = _apply_rewrites(fuse(graph), attention, residual, qkv, rope_epilogue)
     return ExecPlan(g, ExecSteps(tuple(Step(o) for o in g.ops)), derived)
 
 
 def rewrite_compiled(compiled, attention: bool = False, residual: bool = False,
-                     qkv: bool = False) -> ExecPlan:
+                     qkv: bool = False, rope_epilogue: bool = False) -> ExecPlan:
     """Apply the CUDA-only rewrites to any compiled pair -- the reference's
     own `Compiled` included -- keeping its plan order for the ops that stay."""
     graph = as_graph(compiled.graph)
     order = [s.op.id for s in compiled.plan.steps if getattr(s, "op", None) is not None]
     by_id = {o.id: o for o in graph.ops}
     g = Graph(graph.tensors, tuple(by_id[i] for i in order), graph.inputs, graph.outputs)
-    g, derived = _apply_rewrites(g, attention, residual, qkv)
+    g, derived = _apply_rewrites(g, attention, residual, qkv, rope_epilogue)
     return ExecPlan(g, ExecSteps(tuple(Step(o) for o in g.ops)), derived)
 
 

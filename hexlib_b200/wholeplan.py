@@ -129,6 +129,35 @@ def _concat_raw(parts, dtype: str, shape, axis: int) -> bytes:
     return np.concatenate(rows, axis=1).tobytes()
 
 
+def rope_segments(cos, sin) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """Cut half-symmetric [T, 64] cos/sin tables (dims i and i + 32 equal, as
+    a rotate-half table built from one frequency list is) into 16-wide
+    segments of dims 0..31 and keep each distinct (cos, sin) segment once:
+    `(seg_cos [2T, 16], seg_sin [2T, 16], seg_idx [T, 2] int32)`, with dims
+    [16s, 16s + 16) and [32 + 16s, 48 + 16s) of token t in row seg_idx[t, s]
+    of both tables (rows past the distinct ones are zero). Segments are
+    compared on their fp32 bits, so every value the GEMM epilogue reads is
+    the table's own. Tables that are not half-symmetric are refused: the
+    rotation then runs as its own op."""
+    c = np.ascontiguousarray(np.asarray(cos, np.float32))
+    s = np.ascontiguousarray(np.asarray(sin, np.float32))
+    if c.ndim != 2 or c.shape != s.shape or c.shape[1] != 64:
+        raise WholePlanError(f"rope tables must be two [T, 64] arrays; got {c.shape}, {s.shape}")
+    cu, su = c.view(np.uint32), s.view(np.uint32)
+    if not (np.array_equal(cu[:, :32], cu[:, 32:]) and np.array_equal(su[:, :32], su[:, 32:])):
+        raise WholePlanError("the RoPE epilogue needs half-symmetric cos/sin tables "
+                             "(dims i and i + 32 equal); compile without rope_epilogue")
+    T = c.shape[0]
+    keys = np.concatenate([cu[:, :32].reshape(2 * T, 16), su[:, :32].reshape(2 * T, 16)], axis=1)
+    uniq, inverse = np.unique(keys, axis=0, return_inverse=True)
+    n = uniq.shape[0]
+    seg_cos = np.zeros((2 * T, 16), np.float32)
+    seg_sin = np.zeros((2 * T, 16), np.float32)
+    seg_cos[:n] = uniq[:, :16].view(np.float32)
+    seg_sin[:n] = uniq[:, 16:].view(np.float32)
+    return seg_cos, seg_sin, inverse.reshape(T, 2).astype(np.int32)
+
+
 def build_cuda_plan(compiled, feeds: Mapping[str, Any] | None = None,
                     alias: bool = False) -> CudaPlan:
     """Pack `compiled`'s whole plan into one blob; stage `feeds`' consts if
@@ -262,17 +291,23 @@ def build_cuda_plan(compiled, feeds: Mapping[str, Any] | None = None,
     derived = dict(getattr(compiled, "derived", {}) or {})
     if feeds is not None:
         payload = bytearray(const_bytes)
+        segments: dict[tuple, tuple] = {}
         for n, p in placements.items():
             if p.region != "const":
                 continue
             if n in derived:
                 how, parts, axis = derived[n]
-                if how != "concat":
+                if how not in ("concat", "rope_segments"):
                     raise WholePlanError(f"const {n!r}: unknown derivation {how!r}")
                 missing = [q for q in parts if q not in feeds]
                 if missing:
                     raise WholePlanError(f"const {n!r} is built from {missing}, not supplied")
-                if p.dtype in quant.BLOCK_BYTES and any(_is_raw(feeds[q]) for q in parts):
+                if how == "rope_segments":
+                    key = tuple(parts)
+                    if key not in segments:
+                        segments[key] = rope_segments(feeds[parts[0]], feeds[parts[1]])
+                    value = segments[key][axis]
+                elif p.dtype in quant.BLOCK_BYTES and any(_is_raw(feeds[q]) for q in parts):
                     value = _concat_raw([feeds[q] for q in parts], p.dtype, p.shape, axis)
                 else:
                     value = np.concatenate([np.asarray(feeds[q]) for q in parts], axis=axis)

@@ -287,15 +287,21 @@ HEXLIB_B200_API int hexlib_b200_matmul_epilogue_residual_fp16(const void *a, con
                                               int K, int N, int act,
                                               void *stream);
 /* matmul_epilogue whose first `rope_cols` output columns are 64-wide heads
- * rotated by the split-half 2-D RoPE of kernels/rope_2d_fp16/kernel_api.h
- * (token of row r: r % T of the [T, 64] cos/sin tables), applied after the
- * fp16 rounding exactly as rope_2d applies it to a stored q or k. With
- * w = [wq | wk | wv] it is the whole q/k/v projection of a block
- * (hexlib/models/vit.py:168-175) in one GEMM. */
+ * rotated by the split-half 2-D RoPE of kernels/rope_2d_fp16/kernel_api.h,
+ * applied after the fp16 rounding exactly as rope_2d applies it to a stored
+ * q or k. The [T, 64] cos/sin tables must be half-symmetric (dims i and
+ * i + 32 share a value, as in every rotate-half table built from one list of
+ * frequencies) and come in 16-wide segments: dims [16s, 16s + 16) and
+ * [32 + 16s, 48 + 16s) of token t (row r's token is r % T) are row
+ * seg_idx[2t + s] of the [n_seg, 16] fp32 tables seg_cos / seg_sin (indices
+ * clamped to [0, n_seg)); a 2-D RoPE table deduplicates to a few KiB this
+ * way, small enough to stay in L1 while every head reads it. With
+ * w = [wq | wk | wv] it is a block's whole q/k/v projection and RoPE
+ * (hexlib/models/vit.py:168-180) in one GEMM. */
 HEXLIB_B200_API int hexlib_b200_matmul_epilogue_rope_fp16(
-    const void *a, const void *w, const float *bias, const float *costab,
-    const float *sintab, void *out, int M, int K, int N, int act, int rope_cols,
-    int T, void *stream);
+    const void *a, const void *w, const float *bias, const float *seg_cos,
+    const float *seg_sin, const int *seg_idx, int n_seg, void *out, int M, int K, int N,
+    int act, int rope_cols, int T, void *stream);
 /* rope_2d (kernels/rope_2d_fp16/kernel_api.h:120-121) applied to the q and
  * k sections of a packed [rows, 3, H, D] projection, token of row r = r % T
  * of the [T, D] tables; the v section is left as it is. out may equal qkv

@@ -8,9 +8,12 @@ import json
 import os
 from collections import Counter
 
+import numpy as np
 import pytest
 
+from hexlib_b200 import feeds as F
 from hexlib_b200 import graph as G
+from hexlib_b200 import wholeplan
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 PLANS = json.load(open(os.path.join(GOLDEN, "plans.json")))
@@ -93,6 +96,54 @@ def test_rewrites_apply_to_a_reference_compiled_pair():
     c = Counter(o.kind for o in rw.graph.ops)
     assert c["attention"] == 2 and c["matmul_epilogue_residual"] == 4
     assert rw.graph.problems() == []
+
+
+def test_rope_epilogue_rewrite_moves_the_rotation_into_the_qkv_gemm():
+    ep = G.compile_for_cuda(G.build_vision_encoder(G.qwen35_at(256)), residual=True, qkv=True,
+                            rope_epilogue=True)
+    c = Counter(o.kind for o in ep.graph.ops)
+    assert c["matmul_epilogue_rope"] == 12 and c["attention_qkv"] == 12
+    assert c["rope_qk"] == 0 and c["rope_2d"] == 0 and c["transpose"] == 0
+    assert c["matmul_epilogue"] == 12 + 3
+    # 12 concatenated weights and biases, one set of segment tables for all blocks
+    assert len(ep.derived) == 24 + 3
+    for o in ep.graph.ops:
+        if o.kind == "matmul_epilogue_rope":
+            assert o.attrs == {"act": "none", "rope_cols": 2 * 12 * 64}
+            assert ep.graph.tensors[o.outputs[0]].shape == (256, 3, 12, 64)
+            segs = [ep.graph.tensors[n] for n in o.inputs[3:]]
+            assert [(t.dtype, t.shape) for t in segs] == [
+                ("fp32", (512, 16)), ("fp32", (512, 16)), ("int32", (256, 2))]
+            assert all(ep.derived[n][0] == "rope_segments" for n in o.inputs[3:])
+    assert ep.graph.problems() == []
+    # a quantized weight keeps the separate rotation
+    q = G.compile_for_cuda(G.build_vision_encoder(G.qwen35_at(256, weight_dtype="q4_0")),
+                           residual=True, qkv=True, rope_epilogue=True)
+    assert Counter(o.kind for o in q.graph.ops)["rope_qk"] == 12
+
+
+def test_rope_segments_rebuild_the_tables_exactly():
+    cfg = G.qwen35_at(512)
+    w = F.weights(cfg, 0, G.build_vision_encoder(cfg))
+    cos, sin = w["rope_cos"], w["rope_sin"]
+    seg_cos, seg_sin, idx = wholeplan.rope_segments(cos, sin)
+    T = cos.shape[0]
+    assert idx.dtype == np.int32 and idx.shape == (T, 2) and seg_cos.shape == (2 * T, 16)
+    half = seg_cos[idx].reshape(T, 32)
+    np.testing.assert_array_equal(np.concatenate([half, half], 1), cos)
+    half = seg_sin[idx].reshape(T, 32)
+    np.testing.assert_array_equal(np.concatenate([half, half], 1), sin)
+    # a 32 x 32 grid repeats each segment along a row or a column of patches
+    assert idx.max() + 1 <= 64
+    ang = np.random.default_rng(0).uniform(-3, 3, (50, 32)).astype(np.float32)
+    ang = np.concatenate([ang, ang], 1)
+    sc, ss, ix = wholeplan.rope_segments(np.cos(ang), np.sin(ang))
+    np.testing.assert_array_equal(sc[ix].reshape(50, 32), np.cos(ang)[:, :32])
+    with pytest.raises(wholeplan.WholePlanError):
+        wholeplan.rope_segments(np.zeros((4, 32), np.float32), np.zeros((4, 32), np.float32))
+    ang[3, 40] += 1.0                       # no longer half-symmetric
+    with pytest.raises(wholeplan.WholePlanError):
+        wholeplan.rope_segments(np.cos(ang), np.sin(ang))
 
 
 def test_invalid_configs_are_refused():

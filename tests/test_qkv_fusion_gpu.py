@@ -20,22 +20,33 @@ def r16(shape, seed, scale=1.0):
     return (np.random.default_rng(seed).standard_normal(shape) * scale).astype(np.float16)
 
 
-@pytest.mark.parametrize("T,H,n_img", [(256, 12, 2), (64, 4, 3), (1024, 12, 1)])
-def test_rope_gemm_equals_three_projections_then_rope(T, H, n_img):
+@pytest.mark.parametrize("T,H,n_img,grid", [(256, 12, 2, False), (64, 4, 3, False),
+                                             (1024, 12, 1, False), (1024, 12, 4, True),
+                                             (256, 16, 3, True)])
+def test_rope_gemm_equals_three_projections_then_rope(T, H, n_img, grid):
     D, K = 64, H * 64
     M = T * n_img
     a = r16((M, K), 1)
     ws = [r16((K, H * D), 2 + i, 0.05) for i in range(3)]
     bs = [(np.random.default_rng(5 + i).standard_normal(H * D) * 0.02).astype(np.float32)
           for i in range(3)]
-    ang = np.random.default_rng(9).uniform(-3, 3, (T, D)).astype(np.float32)
-    cos, sin = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+    ang = np.random.default_rng(9).uniform(-3, 3, (T, D // 2)).astype(np.float32)
     w = np.concatenate(ws, 1)
     b = np.concatenate(bs)
+    if grid:
+        # a 2-D table: dims [0,16) follow the patch row, [16,32) its column
+        side = int(round(T ** 0.5))
+        r, c = np.divmod(np.arange(T), side)
+        ang = np.concatenate([ang[r, :16], ang[c, 16:]], 1)
+    ang = np.concatenate([ang, ang], 1)       # rotate-half tables: dims i, i + 32 equal
+    cos, sin = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+    seg_cos, seg_sin, seg_idx = wholeplan.rope_segments(cos, sin)
+    n_seg = int(seg_idx.max()) + 1
     y = U.empty((M, 3 * H * D), np.float16)
-    da, dw, db, dc, ds = U.dev(a), U.dev(w), U.dev(b), U.dev(cos), U.dev(sin)
+    da, dw, db = U.dev(a), U.dev(w), U.dev(b)
+    dc, ds, dx = U.dev(seg_cos[:n_seg]), U.dev(seg_sin[:n_seg]), U.dev(seg_idx)
     U.call("hexlib_b200_matmul_epilogue_rope_fp16", U.ptr(da), U.ptr(dw), U.ptr(db), U.ptr(dc),
-           U.ptr(ds), U.ptr(y), M, K, 3 * H * D, 0, 2 * H * D, T, U.stream())
+           U.ptr(ds), U.ptr(dx), n_seg, U.ptr(y), M, K, 3 * H * D, 0, 2 * H * D, T, U.stream())
     got = U.host(y).reshape(n_img, T, 3, H, D)
     af = a.astype(np.float32)
     for i, which in enumerate("qkv"):
@@ -104,14 +115,16 @@ def test_packed_attention_refuses_what_it_cannot_serve():
     assert U.call_rc("hexlib_b200_attention_qkv_fp16", 0, 0, 1, 64, 2, 64, -1.0, 0) == 6
 
 
-def test_fully_fused_encoder_matches_the_oracle():
+@pytest.mark.parametrize("rope_epilogue", [False, True])
+def test_fully_fused_encoder_matches_the_oracle(rope_epilogue):
     cfg = G.qwen35_at(256)
     g = G.build_vision_encoder(cfg)
     w = F.weights(cfg, 0, g)
     imgs = F.images(cfg, 2, 21)
-    ep = G.compile_for_cuda(g, residual=True, qkv=True)
+    ep = G.compile_for_cuda(g, residual=True, qkv=True, rope_epilogue=rope_epilogue)
     plan = wholeplan.build_cuda_plan(ep, w, alias=True)
     assert plan.kinds.count("attention_qkv") == 12
+    assert plan.kinds.count("matmul_epilogue_rope") == (12 if rope_epilogue else 0)
     with Session(0) as s:
         s.load(plan, max_images=2)
         out = s.run(np.ascontiguousarray(imgs))
