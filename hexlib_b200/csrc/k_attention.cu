@@ -298,24 +298,30 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         // p = 2^(s*c - m), 32 keys at a time: one FMA and one MUFU exponential
         // per key, eight partial row sums, and the fp16 pairs stored to this
         // row's lane of P in TMEM (column e holds keys 2e and 2e + 1).
-        float ps[8];
+        // (pairs of keys through sm_100's two-wide FMA and add: the same
+        // roundings as two scalar operations, half the instructions)
+        const float2 c2 = make_float2(c, c), nm2 = make_float2(-m_use, -m_use);
+        float2 ps[4];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) ps[e] = 0.f;
+        for (int e = 0; e < 4; ++e) ps[e] = make_float2(0.f, 0.f);
 #pragma unroll
         for (int k32 = 0; k32 < AT_BN / 32; ++k32) {
           uint32_t h2[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
             const int x = k32 * 32 + 2 * e;
-            const float p0 = ex2_approx(fmaf(__uint_as_float(sv[x]), c, -m_use));
-            const float p1 = ex2_approx(fmaf(__uint_as_float(sv[x + 1]), c, -m_use));
-            ps[(2 * e) & 7] += p0;
-            ps[(2 * e + 1) & 7] += p1;
+            const float2 a = __ffma2_rn(make_float2(__uint_as_float(sv[x]),
+                                                    __uint_as_float(sv[x + 1])), c2, nm2);
+            const float p0 = ex2_approx(a.x);
+            const float p1 = ex2_approx(a.y);
+            ps[e & 3].x += p0;
+            ps[e & 3].y += p1;
             h2[e] = pack_half2(p0, p1);
           }
           tmem_st_32x32b_x16(p_col + (uint32_t)(k32 * 16), h2);
         }
-        const float rs = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+        const float rs = ((ps[0].x + ps[0].y) + (ps[1].x + ps[1].y)) +
+                         ((ps[2].x + ps[2].y) + (ps[3].x + ps[3].y));
         // O *= alpha before P V of this block is issued (rare: the max grew by
         // more than 2^8 since the last rescale)
         if (j > 0 && __any_sync(0xffffffffu, rescale)) {
