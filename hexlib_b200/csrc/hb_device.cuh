@@ -69,25 +69,40 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// The same test, but a thread whose phase is not yet complete is suspended
+// until it completes or kSuspendNs pass, instead of spinning: a waiting warp
+// then takes no issue slots from the warps that share its scheduler.
+constexpr uint32_t kSuspendNs = 20000;
+
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for the phase with `parity` to complete. Returns false if the shared
 // abort flag was raised by another role or `limit_ns` passed; in the latter
 // case the first thread to notice raises the abort flag and records the
-// error, so every other role stops at its next wait.
+// error, so every other role stops at its next wait. Each round suspends for
+// at most kSuspendNs, so both are checked at least that often.
 __device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity,
                                                 volatile int* abort_flag,
                                                 int* err, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
-  uint32_t n = 0;
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((++n & 63u) == 0) {
-      if (*abort_flag) return false;
-      if (global_timer_ns() - t0 > limit_ns) {
-        *abort_flag = 1;
-        if (err) atomicExch(err, HB_DEVERR_WAIT_TIMEOUT);
-        return false;
-      }
+    if (mbar_try_wait_suspend(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (global_timer_ns() - t0 > limit_ns) {
+      *abort_flag = 1;
+      if (err) atomicExch(err, HB_DEVERR_WAIT_TIMEOUT);
+      return false;
     }
   }
 }
@@ -142,22 +157,32 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t pa
   return ok != 0;
 }
 
+// mbar_try_wait_cluster, suspending as mbar_try_wait_suspend does.
+__device__ __forceinline__ bool mbar_try_wait_cluster_suspend(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
+      : "memory");
+  return ok != 0;
+}
+
 // mbar_wait with cluster-scope acquire, for barriers arrived on from the
 // other CTA of a pair. Same limit and abort protocol as mbar_wait_limit.
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
                                                   volatile int* abort_flag, int* err) {
   if (mbar_try_wait_cluster(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
-  uint32_t n = 0;
   while (true) {
-    if (mbar_try_wait_cluster(bar, parity)) return true;
-    if ((++n & 63u) == 0) {
-      if (*abort_flag) return false;
-      if (global_timer_ns() - t0 > HB_WAIT_LIMIT_NS) {
-        *abort_flag = 1;
-        if (err) atomicExch(err, HB_DEVERR_WAIT_TIMEOUT);
-        return false;
-      }
+    if (mbar_try_wait_cluster_suspend(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (global_timer_ns() - t0 > HB_WAIT_LIMIT_NS) {
+      *abort_flag = 1;
+      if (err) atomicExch(err, HB_DEVERR_WAIT_TIMEOUT);
+      return false;
     }
   }
 }

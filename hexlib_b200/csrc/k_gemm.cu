@@ -154,7 +154,12 @@ __device__ __forceinline__ void rope_row(const GemmParams& p, int64_t tok, float
 // time, finished in registers (bias, GELU, residual, rounding), written to
 // this warp's 128B-swizzled staging box and stored by one TMA store, which
 // also clips the tile's row and column tails.
-template <bool ROPE>
+//
+// RES_SMEM: the residual was brought into the warp's staging boxes by TMA
+// (one 4 KiB box per group, same swizzle as the output) before the
+// accumulator was ready; each group is finished in its own box, in place, so
+// no group waits for the previous group's store.
+template <bool ROPE, bool RES_SMEM = false>
 __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtensorMap* tmC,
                                               uint32_t tacc, uint8_t* stage, int quarter,
                                               int lane, int g_lo, int g_hi, int64_t b,
@@ -162,9 +167,10 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
   const int64_t row = row0 + quarter * 32 + lane;
   const bool row_ok = row < p.M;
   const uint32_t trow = tacc + ((uint32_t)(quarter * 32) << 16);
-  // (the RoPE kernels take no residual)
-  const __half* rrow =
-      (!ROPE && p.resid && row_ok) ? p.resid + (b * p.M + row) * (int64_t)p.N : nullptr;
+  // (the RoPE kernels take no residual; RES_SMEM reads it from shared memory)
+  const __half* rrow = (!ROPE && !RES_SMEM && p.resid && row_ok)
+                           ? p.resid + (b * p.M + row) * (int64_t)p.N
+                           : nullptr;
   // the row's cos / sin, loaded once for every head of the tile
   float rc[32], rs[32];
   const bool rope_row_ok = ROPE && row_ok && n0 + g_lo * 64 < p.rope_cols;
@@ -196,9 +202,12 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
   if (rrow && g_lo < g_hi) load_res(g_lo, 0, res[0]);
 #pragma unroll 1
   for (int g = g_lo; g < g_hi; ++g) {
-    // the previous group's store must have finished reading the stage
-    if (lane == 0) bulk_wait_read_all();
-    __syncwarp();
+    uint8_t* box = RES_SMEM ? stage + (g - g_lo) * 4096 : stage;
+    if constexpr (!RES_SMEM) {
+      // the previous group's store must have finished reading the stage
+      if (lane == 0) bulk_wait_read_all();
+      __syncwarp();
+    }
     uint32_t packed[2][16];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -237,10 +246,18 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
         for (int j = 0; j < 32; ++j) v[j] = gelu_erf_f(v[j]);
       }
       uint32_t hw[16];
-      if (rrow) {
+      if constexpr (RES_SMEM) {
+        // this row's 64 bytes of the chunk, at their swizzled places
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const __half2* rh = reinterpret_cast<const __half2*>(&res[h][j]);
+          const int chunk = (h * 4 + j) ^ (rl & 7);
+          res[0][j] = *reinterpret_cast<const uint4*>(box + rl * 128 + chunk * 16);
+        }
+      }
+      if (rrow || RES_SMEM) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const __half2* rh = reinterpret_cast<const __half2*>(&res[RES_SMEM ? 0 : h][j]);
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             // The matmul result is an fp16 tensor in the unfused plan:
@@ -267,14 +284,14 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int chunk = (h * 4 + j) ^ (rl & 7);
-        *reinterpret_cast<uint4*>(stage + rl * 128 + chunk * 16) =
+        *reinterpret_cast<uint4*>(box + rl * 128 + chunk * 16) =
             make_uint4(packed[h][4 * j], packed[h][4 * j + 1], packed[h][4 * j + 2],
                        packed[h][4 * j + 3]);
       }
     fence_proxy_async_shared();
     __syncwarp();
     if (lane == 0) {
-      tma_store_3d(tmC, stage, n0 + g * 64, (int)(row0 + quarter * 32), (int)b);
+      tma_store_3d(tmC, box, n0 + g * 64, (int)(row0 + quarter * 32), (int)b);
       bulk_commit_group();
     }
   }
@@ -457,24 +474,37 @@ done:
 //
 // A wait that gives up raises the abort flag of both CTAs, so the pair
 // unwinds together and meets at the closing cluster barrier.
+//
+// Epilogue modes: kPairPlain (bias, activation, or a residual read from
+// global memory), kPairRope, and kPairRes: each epilogue warp TMA-loads its
+// two 32x64 residual boxes into its staging (8 KiB per warp, one fewer
+// stage) as soon as the previous tile's stores have read it -- before the
+// accumulator is ready -- so the residual's DRAM latency hides under the
+// mainloop instead of stalling the epilogue.
+enum { kPairPlain = 0, kPairRope = 1, kPairRes = 2 };
+
+template <int MODE>
 struct PairCfg {
   static constexpr int BN = 256;                     // columns of the pair's tile
-  static constexpr int STAGES = 6;
+  static constexpr int STAGES = MODE == kPairRes ? 5 : 6;
   static constexpr int A_BYTES = BM * BK * 2;        // 16 KiB: this CTA's 128 rows
   static constexpr int B_BYTES = (BN / 2) * BK * 2;  // 16 KiB: this CTA's 128 columns
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;           // two fp32 accumulators
-  static constexpr int STAGING = kEpiWarps * 4096;
+  static constexpr int STAGING = kEpiWarps * (MODE == kPairRes ? 8192 : 4096);
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGING + 1024 + 256;
 };
 
-template <bool ROPE>
+template <int MODE>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_f16_pair(const __grid_constant__ CUtensorMap tmA,
                   const __grid_constant__ CUtensorMap tmB,
-                  const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
-  using Cfg = PairCfg;
+                  const __grid_constant__ CUtensorMap tmC,
+                  const __grid_constant__ CUtensorMap tmR, const GemmParams p) {
+  using Cfg = PairCfg<MODE>;
   constexpr int BN = Cfg::BN;
+  constexpr bool ROPE = MODE == kPairRope;
+  constexpr bool RES = MODE == kPairRes;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -485,7 +515,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* empty = full + Cfg::STAGES;
   uint64_t* tfull = empty + Cfg::STAGES;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* rfull = tempty + 2;                      // [kEpiWarps], kPairRes only
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rfull + kEpiWarps);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -502,6 +533,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 2 * kEpiWarps);
     }
+    for (int w = 0; w < kEpiWarps; ++w) mbar_init(&rfull[w], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -509,6 +541,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
     tma_prefetch_desc(&tmC);
+    if (RES) tma_prefetch_desc(&tmR);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
@@ -603,22 +636,42 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     constexpr int kGroups = BN / 64;
     const int g_lo = colhalf * (kGroups / 2);
     const int g_hi = (colhalf + 1) * (kGroups / 2);
-    uint8_t* stage = sOut + ew * 4096;
+    uint8_t* stage = sOut + ew * (Cfg::STAGING / kEpiWarps);
     int acc = 0;
     uint32_t acc_phase = 0;
+    uint32_t r_phase = 0;
     for (int64_t t = pair_id; t < p.total_tiles; t += n_pairs) {
       const int64_t b = t / tiles_per_batch;
       const int64_t r = t - b * tiles_per_batch;
       const int mb = (int)(r / p.tiles_n);
       const int nb = (int)(r % p.tiles_n);
+      const int64_t row0 = (int64_t)mb * (2 * BM) + rank * BM;
+      if constexpr (RES) {
+        if (lane == 0) {
+          // the previous tile's stores have read the boxes: refill them
+          bulk_wait_read_all();
+          mbar_arrive_expect_tx(&rfull[ew], 2 * 4096);
+          for (int gi = 0; gi < 2; ++gi)
+            tma_load_3d(&tmR, &rfull[ew], stage + gi * 4096, nb * BN + (g_lo + gi) * 64,
+                        (int)(row0 + quarter * 32), (int)b);
+        }
+      }
       const bool ok = mbar_wait_cluster(&tfull[acc], acc_phase, abort_flag, p.err);
       if (!__all_sync(0xffffffffu, ok)) {
         if (lane == 0) st_cluster_u32(peer_abort, 1);
         goto done;
       }
       tc_fence_after();
-      epilogue_tile<ROPE>(p, &tmC, tmem_base + (uint32_t)(acc * BN), stage, quarter, lane,
-                           g_lo, g_hi, b, (int64_t)mb * (2 * BM) + rank * BM, nb * BN);
+      if constexpr (RES) {
+        const bool rok = mbar_wait(&rfull[ew], r_phase, abort_flag, p.err);
+        r_phase ^= 1u;
+        if (!__all_sync(0xffffffffu, rok)) {
+          if (lane == 0) st_cluster_u32(peer_abort, 1);
+          goto done;
+        }
+      }
+      epilogue_tile<ROPE, RES>(p, &tmC, tmem_base + (uint32_t)(acc * BN), stage, quarter,
+                               lane, g_lo, g_hi, b, row0, nb * BN);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_lead + (uint32_t)(acc * 8));
@@ -767,11 +820,13 @@ bool aligned16(const void* p) {
 // Pairs that fit on the device at once (0: the pair kernel is not used),
 // found once by the occupancy calculator for clusters of two.
 int g_pair_clusters = 0;
+bool g_pair_res = false;
 
 template <bool ROPE>
 int launch_pair(const GemmDesc& g, int* err, cudaStream_t s) {
-  using Cfg = PairCfg;
-  CUtensorMap ta, tb, tcm;
+  constexpr int MODE = ROPE ? kPairRope : kPairPlain;
+  using Cfg = PairCfg<MODE>;
+  CUtensorMap ta, tb, tcm, trm;
   // A: dims (K, M, batch); box (64, 128, 1) -- one CTA's rows.
   if (!make_tmap_3d_f16(&ta, g.A, (uint64_t)g.K, (uint64_t)g.M, (uint64_t)g.batch, BK, BM))
     return -1;
@@ -781,6 +836,11 @@ int launch_pair(const GemmDesc& g, int* err, cudaStream_t s) {
     return -1;
   if (!make_tmap_3d_f16(&tcm, g.out, (uint64_t)g.N, (uint64_t)g.M, (uint64_t)g.batch, 64, 32))
     return -1;
+  // the residual, read through TMA boxes shaped like the output's
+  const bool res_tma = !ROPE && g.resid && g_pair_res &&
+                       make_tmap_3d_f16(&trm, g.resid, (uint64_t)g.N, (uint64_t)g.M,
+                                        (uint64_t)g.batch, 64, 32);
+  if (!res_tma) trm = tcm;
   GemmParams p;
   p.M = g.M;
   p.K = g.K;
@@ -807,7 +867,7 @@ int launch_pair(const GemmDesc& g, int* err, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
   cfg.blockDim = dim3(kGemmThreads, 1, 1);
-  cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+  cfg.dynamicSmemBytes = res_tma ? PairCfg<kPairRes>::SMEM_BYTES : Cfg::SMEM_BYTES;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -816,7 +876,10 @@ int launch_pair(const GemmDesc& g, int* err, cudaStream_t s) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, gemm_f16_pair<ROPE>, ta, tb, tcm, p) != cudaSuccess) {
+  const cudaError_t e =
+      res_tma ? cudaLaunchKernelEx(&cfg, gemm_f16_pair<kPairRes>, ta, tb, tcm, trm, p)
+              : cudaLaunchKernelEx(&cfg, gemm_f16_pair<MODE>, ta, tb, tcm, trm, p);
+  if (e != cudaSuccess) {
     cudaGetLastError();
     return HEXLIB_B200_ERR_CUDA;
   }
@@ -851,14 +914,22 @@ int gemm_kernels_init() {
   g_pair_clusters = 0;
   const char* env = getenv("HEXLIB_B200_GEMM_PAIR");
   if (!(env && env[0] == '0') &&
-      cudaFuncSetAttribute(gemm_f16_pair<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           PairCfg::SMEM_BYTES) == cudaSuccess &&
-      cudaFuncSetAttribute(gemm_f16_pair<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           PairCfg::SMEM_BYTES) == cudaSuccess) {
+      cudaFuncSetAttribute(gemm_f16_pair<kPairPlain>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           PairCfg<kPairPlain>::SMEM_BYTES) == cudaSuccess &&
+      cudaFuncSetAttribute(gemm_f16_pair<kPairRope>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           PairCfg<kPairRope>::SMEM_BYTES) == cudaSuccess) {
+    // the TMA-staged residual: HEXLIB_B200_GEMM_PAIR_RES=0 turns it off
+    const char* er = getenv("HEXLIB_B200_GEMM_PAIR_RES");
+    g_pair_res = !(er && er[0] == '0') &&
+                 cudaFuncSetAttribute(gemm_f16_pair<kPairRes>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      PairCfg<kPairRes>::SMEM_BYTES) == cudaSuccess;
+    cudaGetLastError();
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (unsigned)sm_count(), 1, 1);
     cfg.blockDim = dim3(kGemmThreads, 1, 1);
-    cfg.dynamicSmemBytes = PairCfg::SMEM_BYTES;
+    cfg.dynamicSmemBytes = PairCfg<kPairPlain>::SMEM_BYTES;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
@@ -867,7 +938,8 @@ int gemm_kernels_init() {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, gemm_f16_pair<false>, &cfg) == cudaSuccess && n > 0)
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_f16_pair<kPairPlain>, &cfg) == cudaSuccess &&
+        n > 0)
       g_pair_clusters = n;
     cudaGetLastError();
   }
