@@ -453,10 +453,20 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(uint32_t M, uint32_t N,
 // GELU, tanh form (hexlib/graph/opdefs/elementwise.py:110-114), through the
 // identity 0.5*(1 + tanh(u)) = 1 / (1 + exp(-2u)), which has no cancellation
 // near u = 0 and needs one exponential.
+//
+// Written as x / (1 + e^{-2u}), u = sqrt(2/pi) (x + 0.044715 x^3), with
+// e^{-2u} = 2^{-x (c + 0.044715 c x^2)}, c = 2 sqrt(2/pi) log2(e): one FMUL,
+// one FFMA, one FMUL, the hardware's approximate 2^x and reciprocal, one
+// FADD and one FMUL. Large negative x gives 2^(+big) = inf, 1/inf = 0 and
+// the correct limit -0; large positive x gives 2^(-big) = 0 and x.
 __device__ __forceinline__ float gelu_tanh_f(float x) {
-  const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
-  const float u = k0 * (x + 0.044715f * x * x * x);
-  return __fdividef(x, 1.0f + __expf(-2.0f * u));
+  constexpr float c = 2.302208198144325f;          // 2 sqrt(2/pi) log2(e)
+  constexpr float c3 = 0.1029432395800235f;        // 0.044715 c
+  const float w = fmaf(x * x, c3, c);
+  float e, r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-x * w));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + e));
+  return x * r;
 }
 
 // GELU, exact erf form (elementwise.py:117-125).

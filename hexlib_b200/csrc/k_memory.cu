@@ -21,7 +21,7 @@ namespace {
 
 constexpr int kThreads = 256;
 
-int grid_for(int64_t work_items, int threads) {
+int sm_count_cached() {
   static int sm_count = 0;
   if (sm_count == 0) {
     int dev = 0;
@@ -29,8 +29,12 @@ int grid_for(int64_t work_items, int threads) {
     cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev);
     if (sm_count <= 0) sm_count = 148;
   }
+  return sm_count;
+}
+
+int grid_for(int64_t work_items, int threads) {
   int64_t blocks = (work_items + threads - 1) / threads;
-  const int64_t cap = static_cast<int64_t>(sm_count) * 8;
+  const int64_t cap = static_cast<int64_t>(sm_count_cached()) * 8;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
   return static_cast<int>(blocks);
@@ -800,6 +804,45 @@ __global__ void patchify_vec(const float4* __restrict__ img,
   }
 }
 
+// The same move organised by merge block: a CTA takes the merge*merge
+// tokens of one merge block (a contiguous span of the output) and first
+// tabulates, for each output float4 of a token, its source offset from the
+// patch's top-left corner -- so the copy loop has no divisions, which
+// otherwise cost more issue slots than the move itself.
+__global__ void patchify_blocks(const float4* __restrict__ img, float4* __restrict__ out,
+                                int64_t n_blocks, int blocks_per_img, int bw_n, int merge,
+                                int patch, int C, int T, int H, int W4, int fv) {
+  extern __shared__ int src_off[];             // [fv]
+  const int pv = patch / 4;
+  for (int f = threadIdx.x; f < fv; f += blockDim.x) {
+    const int pw4 = f % pv;
+    int q = f / pv;
+    const int ph = q % patch;
+    q /= patch;
+    const int t = q % T;
+    const int c = q / T;
+    src_off[f] = ((c * T + t) * H + ph) * W4 + pw4;
+  }
+  __syncthreads();
+  const int64_t img4 = (int64_t)C * T * H * W4;
+  const int mm = merge * merge;
+  for (int64_t mb = blockIdx.x; mb < n_blocks; mb += gridDim.x) {
+    const int64_t n = mb / blocks_per_img;
+    const int rb = (int)(mb - n * blocks_per_img);
+    const int bh = rb / bw_n, bw = rb - bh * bw_n;
+    const float4* src_n = img + n * img4;
+    float4* dst = out + mb * mm * (int64_t)fv;
+    for (int m = 0; m < mm; ++m) {
+      const int mh = m / merge, mw = m - mh * merge;
+      const float4* src =
+          src_n + (int64_t)((bh * merge + mh) * patch) * W4 + (bw * merge + mw) * pv;
+      float4* d = dst + (int64_t)m * fv;
+#pragma unroll 4
+      for (int f = threadIdx.x; f < fv; f += blockDim.x) d[f] = __ldg(src + src_off[f]);
+    }
+  }
+}
+
 __global__ void patchify_scalar(const float* __restrict__ img,
                                 float* __restrict__ out, int64_t nimg, int C,
                                 int T, int H, int W, int patch, int merge,
@@ -1131,7 +1174,18 @@ int launch_patchify_f32(const float* img, float* out, int64_t nimg, int C,
   if (nimg == 0) return HEXLIB_B200_OK;
   const int64_t total =
       nimg * (int64_t)grid_h * grid_w * C * T * patch * patch;
-  if ((patch % 4) == 0 && aligned16(img) && aligned16(out)) {
+  const int fv = C * T * patch * patch / 4;
+  if ((patch % 4) == 0 && aligned16(img) && aligned16(out) && fv <= 8192 &&
+      (int64_t)C * T * H * W < ((int64_t)1 << 31)) {
+    const int bw_n = grid_w / merge;
+    const int per_img = (grid_h / merge) * bw_n;
+    const int64_t n_blocks = nimg * per_img;
+    const int64_t cap = (int64_t)sm_count_cached() * 16;
+    patchify_blocks<<<(unsigned)(n_blocks < cap ? n_blocks : cap), 128,
+                      (size_t)fv * sizeof(int), s>>>(
+        (const float4*)img, (float4*)out, n_blocks, per_img, bw_n, merge, patch, C, T, H,
+        W / 4, fv);
+  } else if ((patch % 4) == 0 && aligned16(img) && aligned16(out)) {
     patchify_vec<<<grid_for(total / 4, kThreads), kThreads, 0, s>>>(
         (const float4*)img, (float4*)out, nimg, C, T, H, W, patch, merge,
         grid_w);
