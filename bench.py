@@ -55,6 +55,8 @@ def parse():
     ap.add_argument("--no-qkv-fusion", action="store_true")
     ap.add_argument("--rope", choices=("epilogue", "pass"), default="epilogue",
                     help="packed qkv path: RoPE in the qkv GEMM's epilogue, or its own pass")
+    ap.add_argument("--ln-fold", choices=("on", "off"), default="off",
+                    help="fold each layernorm that feeds a GEMM into that GEMM's epilogue")
     ap.add_argument("--weights", choices=("fp16", "q4_0", "q8_0"), default="fp16",
                     help="matmul weight dtype (q4_0 is the reference model's own)")
     ap.add_argument("--sweep", action="store_true",
@@ -228,7 +230,8 @@ def op_work(plan, op_index: int, n_images: int) -> tuple[str, float, str]:
         p = P[names[n]]
         return p.nbytes * (n_images if p.buffer == 1 else 1)
 
-    if vname in ("matmul_epilogue", "matmul_epilogue_residual"):
+    if vname in ("matmul_epilogue", "matmul_epilogue_residual", "matmul_epilogue_ln",
+                 "matmul_epilogue_ln_rope"):
         a, w = P[names[srcs[0]]], P[names[srcs[1]]]
         M = a.shape[0] * n_images
         K, N = w.shape
@@ -275,7 +278,8 @@ def run_b200(args) -> None:
     use_att = (not args.no_attention_fusion) and attention_available()
     use_qkv = use_att and not args.no_qkv_fusion
     ep = G.compile_for_cuda(g, attention=use_att, residual=not args.no_residual_fusion,
-                            qkv=use_qkv, rope_epilogue=args.rope == "epilogue")
+                            qkv=use_qkv, rope_epilogue=args.rope == "epilogue",
+                            ln_fold=args.ln_fold == "on" and args.weights == "fp16")
     w = F.weights(cfg, 0, g)
     plan = wholeplan.build_cuda_plan(ep, w, alias=True)
     sh = D.shard(args.batch, rank, world)
@@ -434,6 +438,7 @@ def run_b200(args) -> None:
                 "seq_len": cfg.num_tokens, "parallelism": f"image-sharded x{world}",
                 "weights": args.weights, "plan_ops": plan.n_ops, "fusions": {"attention": use_att, "qkv_rope": use_qkv,
                                                    "rope": args.rope if use_qkv else None,
+                                                   "ln_fold": args.ln_fold == "on",
                                                    "residual": not args.no_residual_fusion},
                 "l2": f"inputs larger than L2: each step reads {plan.const_bytes / 1e6:.0f} MB "
                       f"of consts and {n * 6.29:.0f} MB of images per GPU",

@@ -370,6 +370,59 @@ int check_op(const OpRec& op) {
         return HEXLIB_B200_ERR_INVAL_PARAMS;
       return HEXLIB_B200_OK;
     }
+    case HEXLIB_B200_KIND_LN_STATS: {
+      // x [R, C] fp16 -> stats [R, 2] fp32; params: eps
+      HB_TRY(need(op, 2));
+      HB_TRY(dt(op, 0, DT_FP16));
+      HB_TRY(dt(op, 1, DT_FP32));
+      HB_TRY(batching(op, 1));
+      const uint32_t* x = op.a[0].ne;
+      const uint32_t* y = op.a[1].ne;
+      if (x[2] != 1 || x[3] != 1 || x[1] == 0 || y[0] != x[0] || y[1] != 2 || y[2] != 1 ||
+          y[3] != 1)
+        return HEXLIB_B200_ERR_INVAL_PARAMS;
+      return HEXLIB_B200_OK;
+    }
+    case HEXLIB_B200_KIND_MATMUL_EPILOGUE_LN:
+    case HEXLIB_B200_KIND_MATMUL_EPILOGUE_LN_ROPE: {
+      // x [M, K], w [K, N] fp16, cols [2, N] fp32 (bias; column sums of w),
+      // stats [M, 2] fp32, (RoPE: segtab [n, 2, 16] fp32, seg_idx [T, 2]
+      // int32,) out [M, N] fp16; params: act (, rope_cols)
+      const bool rope = op.kind == HEXLIB_B200_KIND_MATMUL_EPILOGUE_LN_ROPE;
+      const uint32_t nb = rope ? 7 : 5;
+      HB_TRY(need(op, nb));
+      HB_TRY(dt(op, 0, DT_FP16));
+      HB_TRY(dt(op, 1, DT_FP16));
+      HB_TRY(dt(op, 2, DT_FP32));
+      HB_TRY(dt(op, 3, DT_FP32));
+      if (rope) {
+        HB_TRY(dt(op, 4, DT_FP32));
+        HB_TRY(dt(op, 5, DT_INT32));
+      }
+      HB_TRY(dt(op, nb - 1, DT_FP16));
+      HB_TRY(batching(op, nb - 1));
+      const uint32_t* a = op.a[0].ne;
+      const uint32_t* w = op.a[1].ne;
+      const uint32_t* c = op.a[2].ne;
+      const uint32_t* st = op.a[3].ne;
+      if (a[2] != 1 || a[3] != 1 || w[2] != 1 || w[3] != 1 || w[0] != a[1] || a[1] == 0 ||
+          w[1] == 0 || w[1] % 256 || c[0] != 2 || c[1] != w[1] || c[2] != 1 || c[3] != 1 ||
+          st[0] != a[0] || st[1] != 2 || st[2] != 1 || st[3] != 1 || op.a[1].per_image ||
+          op.a[2].per_image || op.a[3].per_image != op.a[0].per_image ||
+          numel(op.a[nb - 1].ne) != (uint64_t)a[0] * w[1])
+        return HEXLIB_B200_ERR_INVAL_PARAMS;
+      if (op.params[0] < 0 || op.params[0] > 2) return HEXLIB_B200_ERR_INVAL_PARAMS;
+      if (rope) {
+        const uint32_t* t = op.a[4].ne;   // n_seg, 2, 16
+        const uint32_t* x = op.a[5].ne;   // T, 2
+        if (op.a[4].per_image || op.a[5].per_image || t[0] == 0 || t[1] != 2 ||
+            t[2] != 16 || t[3] != 1 || x[0] == 0 || x[1] != 2 || x[2] != 1 || x[3] != 1 ||
+            a[0] % x[0] != 0 || op.params[1] <= 0 || op.params[1] % 64 ||
+            (uint32_t)op.params[1] > w[1])
+          return HEXLIB_B200_ERR_INVAL_PARAMS;
+      }
+      return HEXLIB_B200_OK;
+    }
     case HEXLIB_B200_KIND_ROPE_QK: {
       HB_TRY(need(op, 4));
       HB_TRY(dt(op, 0, DT_FP16));
@@ -535,6 +588,36 @@ int run_op(const OpRec& op, uint32_t n_images, int* err, void* ws, uint64_t ws_b
       g.rope_nseg = (int)a[3].ne[0];
       g.rope_T = (int)a[5].ne[0];
       g.rope_cols = op.params[1];
+      return hb::launch_gemm(g, err, s);
+    }
+    case HEXLIB_B200_KIND_LN_STATS:
+      return hb::launch_ln_stats_f16(a[0].ptr, (float*)a[1].ptr, (int64_t)a[0].ne[0] * B,
+                                     (int)a[0].ne[1], param_f(op, 0), s);
+    case HEXLIB_B200_KIND_MATMUL_EPILOGUE_LN:
+    case HEXLIB_B200_KIND_MATMUL_EPILOGUE_LN_ROPE: {
+      const bool rope = op.kind == HEXLIB_B200_KIND_MATMUL_EPILOGUE_LN_ROPE;
+      hb::GemmDesc g{};
+      g.A = a[0].ptr;
+      g.B = a[1].ptr;
+      g.N = (int)a[1].ne[1];
+      g.bias = (const float*)a[2].ptr;
+      g.ln_colsum = (const float*)a[2].ptr + g.N;
+      g.ln_stats = (const float*)a[3].ptr;
+      g.out = a[rope ? 6 : 4].ptr;
+      g.batch = 1;
+      g.M = (int64_t)a[0].ne[0] * B;
+      g.K = (int)a[0].ne[1];
+      g.b_shared = true;
+      g.act = op.params[0];
+      if (rope) {
+        g.rope_cos = (const float*)a[4].ptr;
+        g.rope_sin = (const float*)a[4].ptr + 16;
+        g.rope_stride = 32;
+        g.rope_idx = (const int*)a[5].ptr;
+        g.rope_nseg = (int)a[4].ne[0];
+        g.rope_T = (int)a[5].ne[0];
+        g.rope_cols = op.params[1];
+      }
       return hb::launch_gemm(g, err, s);
     }
     case HEXLIB_B200_KIND_ROPE_QK:

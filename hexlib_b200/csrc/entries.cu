@@ -291,6 +291,62 @@ int hexlib_b200_matmul_epilogue_rope_fp16(const void* a, const void* w, const fl
   return hb::launch_gemm(g, hb::default_error_word(), as_stream(stream));
 }
 
+int hexlib_b200_ln_stats_fp16(const void* x, float* stats, int R, int C, float eps,
+                              void* stream) {
+  HB_ENTRY_INIT();
+  return hb::launch_ln_stats_f16(x, stats, R, C, eps, as_stream(stream));
+}
+
+static int matmul_ln(const void* x, const void* w, const float* cols, const float* stats,
+                     const float* segtab, const int* seg_idx, int n_seg, void* out, int M,
+                     int K, int N, int act, int rope_cols, int T, void* stream) {
+  if (M < 0 || K <= 0 || N <= 0 || act < 0 || act > 2 || !cols || !stats)
+    return HEXLIB_B200_ERR_INVAL_PARAMS;
+  hb::GemmDesc g{};
+  g.A = x;
+  g.B = w;
+  g.bias = cols;
+  g.ln_colsum = cols + N;
+  g.ln_stats = stats;
+  g.out = out;
+  g.batch = 1;
+  g.M = M;
+  g.K = K;
+  g.N = N;
+  g.b_shared = true;
+  g.act = act;
+  if (segtab) {
+    if (!seg_idx || n_seg <= 0 || rope_cols <= 0 || T <= 0 || (M % T) != 0)
+      return HEXLIB_B200_ERR_INVAL_PARAMS;
+    g.rope_cos = segtab;
+    g.rope_sin = segtab + 16;
+    g.rope_stride = 32;
+    g.rope_idx = seg_idx;
+    g.rope_nseg = n_seg;
+    g.rope_T = T;
+    g.rope_cols = rope_cols;
+  }
+  return hb::launch_gemm(g, hb::default_error_word(), as_stream(stream));
+}
+
+int hexlib_b200_matmul_epilogue_ln_fp16(const void* x, const void* w, const float* cols,
+                                        const float* stats, void* out, int M, int K, int N,
+                                        int act, void* stream) {
+  HB_ENTRY_INIT();
+  return matmul_ln(x, w, cols, stats, nullptr, nullptr, 0, out, M, K, N, act, 0, 0, stream);
+}
+
+int hexlib_b200_matmul_epilogue_ln_rope_fp16(const void* x, const void* w, const float* cols,
+                                             const float* stats, const float* segtab,
+                                             const int* seg_idx, int n_seg, void* out, int M,
+                                             int K, int N, int act, int rope_cols, int T,
+                                             void* stream) {
+  HB_ENTRY_INIT();
+  if (!segtab) return HEXLIB_B200_ERR_INVAL_PARAMS;
+  return matmul_ln(x, w, cols, stats, segtab, seg_idx, n_seg, out, M, K, N, act, rope_cols, T,
+                   stream);
+}
+
 int hexlib_b200_rope_qk_fp16(const void* qkv, const float* costab, const float* sintab,
                              void* out, int rows, int H, int D, int T, void* stream) {
   HB_ENTRY_INIT();

@@ -30,6 +30,9 @@ int launch_copy(const void* x, void* y, int64_t nbytes, cudaStream_t s);
 // Row-wise.
 int launch_layernorm_f16(const void* x, const float* w, const float* b,
                          void* y, int64_t R, int C, float eps, cudaStream_t s);
+// (mean, 1/sqrt(var + eps)) of each of R rows of C fp16, as float2 pairs.
+int launch_ln_stats_f16(const void* x, float* stats, int64_t R, int C, float eps,
+                        cudaStream_t s);
 int launch_rmsnorm_f16(const void* x, const void* w, void* y, int64_t R, int C,
                        float eps, cudaStream_t s);
 int launch_softmax_f16(const void* x, void* y, int64_t R, int C,
@@ -78,9 +81,20 @@ struct GemmDesc {
   const float* rope_cos = nullptr;
   const float* rope_sin = nullptr;
   const int* rope_idx = nullptr;   // [rope_T, 2]; entries clamped to [0, rope_nseg)
+  // floats between consecutive segment rows: 16 for separate cos / sin
+  // tables, 32 for one [n, 2, 16] table (rope_sin = rope_cos + 16); 0 = 16
+  int rope_stride = 0;
   int rope_nseg = 0;
   int rope_T = 0;
   int rope_cols = 0;
+  // LayerNorm epilogue (tensor-core kernels, N % 256 == 0, no residual):
+  // when ln_stats is set, A holds the raw rows x and B = diag(gamma) W; row
+  // r's (mean, rstd) pair is ln_stats[2r, 2r + 1] (8-byte aligned), the
+  // column sums of B are ln_colsum[N] (16-byte aligned), and the result is
+  // act(rstd * (A@B - mean * colsum) + bias) = act(LayerNorm(x) @ W + bias)
+  // when bias = beta @ W + the original bias.
+  const float* ln_stats = nullptr;
+  const float* ln_colsum = nullptr;
 };
 int launch_gemm(const GemmDesc& g, int* err, cudaStream_t s);
 

@@ -78,8 +78,14 @@ struct GemmParams {
   const float* rope_sin;
   const int* rope_idx;
   int rope_nseg;
+  int rope_stride;   // floats from one segment row to the next (16, or 32 interleaved)
   int rope_T;
   int rope_cols;
+  // LayerNorm epilogue (LN kernels only): row r's (mean, rstd) at
+  // ln_stats[2 r], the column sums of the folded weight at ln_colsum[n];
+  // the value is rstd * (acc - mean * colsum) + bias.
+  const float* ln_stats;
+  const float* ln_colsum;
 };
 
 // One whole 32-byte sector per thread (sm_100's 256-bit load): a residual
@@ -133,8 +139,8 @@ __device__ __forceinline__ void rope_row(const GemmParams& p, int64_t tok, float
   ix.y = min(max(ix.y, 0), top);
 #pragma unroll
   for (int s = 0; s < 2; ++s) {
-    const float* cp = p.rope_cos + (s ? ix.y : ix.x) * 16;
-    const float* sp = p.rope_sin + (s ? ix.y : ix.x) * 16;
+    const float* cp = p.rope_cos + (s ? ix.y : ix.x) * p.rope_stride;
+    const float* sp = p.rope_sin + (s ? ix.y : ix.x) * p.rope_stride;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float4 c = ld_nc_evict_last_f4(cp + 4 * j);
@@ -159,7 +165,12 @@ __device__ __forceinline__ void rope_row(const GemmParams& p, int64_t tok, float
 // (one 4 KiB box per group, same swizzle as the output) before the
 // accumulator was ready; each group is finished in its own box, in place, so
 // no group waits for the previous group's store.
-template <bool ROPE, bool RES_SMEM = false>
+//
+// LN: the A operand was the raw row x and the weight diag(gamma) W; the
+// accumulator is turned into LayerNorm(x) @ W + bias by the row's (mean,
+// rstd) and the weight's column sums: rstd * (acc - mean * colsum) + bias,
+// with bias holding beta @ W + the GEMM's own bias.
+template <bool ROPE, bool RES_SMEM = false, bool LN = false>
 __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtensorMap* tmC,
                                               uint32_t tacc, uint8_t* stage, int quarter,
                                               int lane, int g_lo, int g_hi, int64_t b,
@@ -172,6 +183,14 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
                            ? p.resid + (b * p.M + row) * (int64_t)p.N
                            : nullptr;
   // the row's cos / sin, loaded once for every head of the tile
+  float ln_mean = 0.f, ln_rstd = 0.f;
+  if constexpr (LN) {
+    if (row_ok) {
+      const float2 ms = __ldg(reinterpret_cast<const float2*>(p.ln_stats) + (b * p.M + row));
+      ln_mean = ms.x;
+      ln_rstd = ms.y;
+    }
+  }
   float rc[32], rs[32];
   const bool rope_row_ok = ROPE && row_ok && n0 + g_lo * 64 < p.rope_cols;
   if constexpr (ROPE) {
@@ -219,7 +238,9 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
         else if (g + 1 < g_hi) load_res(g + 1, 0, res[0]);
       }
       float bias[32];
-      if (p.bias && nc < p.N) {
+      if (LN) {
+        // (loaded with the column sums below, next to their use)
+      } else if (p.bias && nc < p.N) {
         const float* bp = p.bias + nc;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -236,11 +257,33 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
       tmem_ld_32x32b_x32(trow + c32, rg);
       tmem_ld_wait();
       float v[32];
+      if constexpr (LN) {
+        // column sums and bias read four at a time next to their use
+        // (both L1-resident)
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(rg[j]) + bias[j];
+        for (int j = 0; j < 32; j += 4) {
+          const bool in = nc + j < p.N;
+          const float4 cs = in ? ld_nc_evict_last_f4(p.ln_colsum + nc + j)
+                               : make_float4(0, 0, 0, 0);
+          const float4 bb = (in && p.bias) ? ld_nc_evict_last_f4(p.bias + nc + j)
+                                           : make_float4(0, 0, 0, 0);
+          const float c4[4] = {cs.x, cs.y, cs.z, cs.w};
+          const float b4[4] = {bb.x, bb.y, bb.z, bb.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            v[j + q] = fmaf(ln_rstd, fmaf(-ln_mean, c4[q], __uint_as_float(rg[j + q])), b4[q]);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(rg[j]) + bias[j];
+      }
       if (p.act == 1) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = gelu_tanh_f(v[j]);
+        for (int j = 0; j < 32; j += 2) {
+          const float2 g = gelu_tanh_f2(make_float2(v[j], v[j + 1]));
+          v[j] = g.x;
+          v[j + 1] = g.y;
+        }
       } else if (p.act == 2) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = gelu_erf_f(v[j]);
@@ -297,7 +340,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
   }
 }
 
-template <int BN, bool ROPE>
+template <int BN, bool ROPE, bool LN = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_f16_tc(const __grid_constant__ CUtensorMap tmA,
                 const __grid_constant__ CUtensorMap tmB,
@@ -434,7 +477,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const bool ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, p.err);
       if (!__all_sync(0xffffffffu, ok)) goto done;
       tc_fence_after();
-      epilogue_tile<ROPE>(p, &tmC, tmem_base + (uint32_t)(acc * BN), stage, quarter, lane,
+      epilogue_tile<ROPE, false, LN>(p, &tmC, tmem_base + (uint32_t)(acc * BN), stage, quarter, lane,
                           g_lo, g_hi, b, (int64_t)mb * BM, nb * BN);
       tc_fence_before();
       __syncwarp();
@@ -481,7 +524,9 @@ done:
 // stage) as soon as the previous tile's stores have read it -- before the
 // accumulator is ready -- so the residual's DRAM latency hides under the
 // mainloop instead of stalling the epilogue.
-enum { kPairPlain = 0, kPairRope = 1, kPairRes = 2 };
+// kPairLn / kPairLnRope: the LayerNorm epilogue (see epilogue_tile), without
+// or with RoPE.
+enum { kPairPlain = 0, kPairRope = 1, kPairRes = 2, kPairLn = 3, kPairLnRope = 4 };
 
 template <int MODE>
 struct PairCfg {
@@ -503,8 +548,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                   const __grid_constant__ CUtensorMap tmR, const GemmParams p) {
   using Cfg = PairCfg<MODE>;
   constexpr int BN = Cfg::BN;
-  constexpr bool ROPE = MODE == kPairRope;
+  constexpr bool ROPE = MODE == kPairRope || MODE == kPairLnRope;
   constexpr bool RES = MODE == kPairRes;
+  constexpr bool LN = MODE == kPairLn || MODE == kPairLnRope;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -670,7 +716,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           goto done;
         }
       }
-      epilogue_tile<ROPE, RES>(p, &tmC, tmem_base + (uint32_t)(acc * BN), stage, quarter,
+      epilogue_tile<ROPE, RES, LN>(p, &tmC, tmem_base + (uint32_t)(acc * BN), stage, quarter,
                                lane, g_lo, g_hi, b, row0, nb * BN);
       tc_fence_before();
       __syncwarp();
@@ -764,7 +810,7 @@ int sm_count() {
   return g_sm_count;
 }
 
-template <int BN, bool ROPE>
+template <int BN, bool ROPE, bool LN = false>
 int launch_tc(const GemmDesc& g, int* err, cudaStream_t s) {
   using Cfg = GemmCfg<BN>;
   CUtensorMap ta, tb;
@@ -800,11 +846,14 @@ int launch_tc(const GemmDesc& g, int* err, cudaStream_t s) {
   p.rope_sin = g.rope_sin;
   p.rope_idx = g.rope_idx;
   p.rope_nseg = g.rope_nseg;
+  p.rope_stride = g.rope_stride > 0 ? g.rope_stride : 16;
   p.rope_T = g.rope_T > 0 ? g.rope_T : 1;
   p.rope_cols = ROPE ? g.rope_cols : 0;
+  p.ln_stats = g.ln_stats;
+  p.ln_colsum = g.ln_colsum;
   const int64_t grid64 =
       p.total_tiles < sm_count() ? p.total_tiles : (int64_t)sm_count();
-  gemm_f16_tc<BN, ROPE><<<(int)grid64, kGemmThreads, Cfg::SMEM_BYTES, s>>>(ta, tb,
+  gemm_f16_tc<BN, ROPE, LN><<<(int)grid64, kGemmThreads, Cfg::SMEM_BYTES, s>>>(ta, tb,
                                                                             tcm, p);
   if (cudaPeekAtLastError() != cudaSuccess) {
     cudaGetLastError();
@@ -822,9 +871,9 @@ bool aligned16(const void* p) {
 int g_pair_clusters = 0;
 bool g_pair_res = false;
 
-template <bool ROPE>
+template <bool ROPE, bool LN = false>
 int launch_pair(const GemmDesc& g, int* err, cudaStream_t s) {
-  constexpr int MODE = ROPE ? kPairRope : kPairPlain;
+  constexpr int MODE = LN ? (ROPE ? kPairLnRope : kPairLn) : (ROPE ? kPairRope : kPairPlain);
   using Cfg = PairCfg<MODE>;
   CUtensorMap ta, tb, tcm, trm;
   // A: dims (K, M, batch); box (64, 128, 1) -- one CTA's rows.
@@ -837,7 +886,7 @@ int launch_pair(const GemmDesc& g, int* err, cudaStream_t s) {
   if (!make_tmap_3d_f16(&tcm, g.out, (uint64_t)g.N, (uint64_t)g.M, (uint64_t)g.batch, 64, 32))
     return -1;
   // the residual, read through TMA boxes shaped like the output's
-  const bool res_tma = !ROPE && g.resid && g_pair_res &&
+  const bool res_tma = !ROPE && !LN && g.resid && g_pair_res &&
                        make_tmap_3d_f16(&trm, g.resid, (uint64_t)g.N, (uint64_t)g.M,
                                         (uint64_t)g.batch, 64, 32);
   if (!res_tma) trm = tcm;
@@ -860,8 +909,11 @@ int launch_pair(const GemmDesc& g, int* err, cudaStream_t s) {
   p.rope_sin = g.rope_sin;
   p.rope_idx = g.rope_idx;
   p.rope_nseg = g.rope_nseg;
+  p.rope_stride = g.rope_stride > 0 ? g.rope_stride : 16;
   p.rope_T = g.rope_T > 0 ? g.rope_T : 1;
   p.rope_cols = ROPE ? g.rope_cols : 0;
+  p.ln_stats = g.ln_stats;
+  p.ln_colsum = g.ln_colsum;
   const int64_t pairs =
       p.total_tiles < g_pair_clusters ? p.total_tiles : (int64_t)g_pair_clusters;
   cudaLaunchConfig_t cfg = {};
@@ -907,6 +959,12 @@ int gemm_kernels_init() {
   cudaError_t e6 = cudaFuncSetAttribute(
       gemm_f16_tc<64, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
       GemmCfg<64>::SMEM_BYTES);
+  cudaError_t e8 = cudaFuncSetAttribute(
+      gemm_f16_tc<256, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      GemmCfg<256>::SMEM_BYTES);
+  cudaError_t e9 = cudaFuncSetAttribute(
+      gemm_f16_tc<256, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      GemmCfg<256>::SMEM_BYTES);
   cudaFuncAttributes fa;
   cudaError_t e7 = cudaFuncGetAttributes(&fa, gemm_f16_simt);
   sm_count();
@@ -919,6 +977,11 @@ int gemm_kernels_init() {
                            PairCfg<kPairPlain>::SMEM_BYTES) == cudaSuccess &&
       cudaFuncSetAttribute(gemm_f16_pair<kPairRope>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            PairCfg<kPairRope>::SMEM_BYTES) == cudaSuccess) {
+    cudaFuncSetAttribute(gemm_f16_pair<kPairLn>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         PairCfg<kPairLn>::SMEM_BYTES);
+    cudaFuncSetAttribute(gemm_f16_pair<kPairLnRope>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         PairCfg<kPairLnRope>::SMEM_BYTES);
     // the TMA-staged residual: HEXLIB_B200_GEMM_PAIR_RES=0 turns it off
     const char* er = getenv("HEXLIB_B200_GEMM_PAIR_RES");
     g_pair_res = !(er && er[0] == '0') &&
@@ -944,7 +1007,8 @@ int gemm_kernels_init() {
     cudaGetLastError();
   }
   if (e1 != cudaSuccess || e2 != cudaSuccess || e3 != cudaSuccess || e4 != cudaSuccess ||
-      e5 != cudaSuccess || e6 != cudaSuccess || e7 != cudaSuccess) {
+      e5 != cudaSuccess || e6 != cudaSuccess || e7 != cudaSuccess || e8 != cudaSuccess ||
+      e9 != cudaSuccess) {
     cudaGetLastError();
     return HEXLIB_B200_ERR_CUDA;
   }
@@ -989,6 +1053,7 @@ int launch_gemm(const GemmDesc& g, int* err, cudaStream_t s) {
   if (g.batch == 0 || g.M == 0) return HEXLIB_B200_OK;
   const bool rope = g.rope_cols > 0;
   if (rope && (g.rope_cols % 64 || g.rope_cols > g.N || g.N % 64 || g.rope_T <= 0 ||
+               (g.rope_stride != 0 && g.rope_stride != 16 && g.rope_stride != 32) ||
                g.rope_nseg <= 0 || !g.rope_cos || !g.rope_sin || !g.rope_idx ||
                !aligned16(g.rope_cos) ||
                !aligned16(g.rope_sin) || !aligned16(g.rope_idx)))
@@ -997,6 +1062,19 @@ int launch_gemm(const GemmDesc& g, int* err, cudaStream_t s) {
                       aligned16(g.B) && aligned16(g.out) &&
                       (!g.bias || aligned16(g.bias)) &&
                       (!g.resid || aligned16(g.resid)) && tma_available();
+  const bool ln = g.ln_stats != nullptr;
+  if (ln && (!g.ln_colsum || g.resid || g.N % 256 || !tma_ok ||
+             (reinterpret_cast<uintptr_t>(g.ln_stats) & 7u) || !aligned16(g.ln_colsum)))
+    return HEXLIB_B200_ERR_INVAL_PARAMS;   // served by the tensor-core kernels only
+  if (ln) {
+    const int tiling = choose_tiling(g);
+    int rc;
+    if (tiling == kTilePair)
+      rc = rope ? launch_pair<true, true>(g, err, s) : launch_pair<false, true>(g, err, s);
+    else
+      rc = rope ? launch_tc<256, true, true>(g, err, s) : launch_tc<256, false, true>(g, err, s);
+    return rc == -1 ? HEXLIB_B200_ERR_INVAL_PARAMS : rc;
+  }
   if (tma_ok) {
     int rc;
     const int tiling = (g.N % 256 == 0) ? choose_tiling(g) : 0;

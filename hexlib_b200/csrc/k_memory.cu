@@ -349,6 +349,44 @@ __global__ void __launch_bounds__(kThreads) layernorm_rows(const uint4* __restri
   }
 }
 
+// The row statistics of layernorm alone: (mean, 1/sqrt(var + eps)) per row,
+// computed exactly as layernorm_rows computes them, for a GEMM that applies
+// the normalisation in its epilogue (the affine weight folded into its
+// matrix). Reads the rows once and writes 8 bytes per row.
+template <int G, int V>
+__global__ void __launch_bounds__(kThreads) ln_stats_rows(const uint4* __restrict__ x,
+                                                          float2* __restrict__ stats, int64_t R,
+                                                          float eps) {
+  constexpr int C = G * V * 8;
+  __shared__ float red[kThreads / 32];
+  const RowWalk<G> rw;
+  uint4 nxt[V];
+  if (rw.first + rw.sub < R) row_load<G, V>(nxt, x, rw.first + rw.sub, rw.g);
+  for (int64_t base = rw.first; base < R; base += rw.step) {
+    const int64_t r = base + rw.sub;
+    float v[V][8];
+    unpack_rows<V>(v, nxt);
+    if (r + rw.step < R) row_load<G, V>(nxt, x, r + rw.step, rw.g);
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < V; ++j)
+#pragma unroll
+      for (int q = 0; q < 8; ++q) s += v[j][q];
+    const float mean = row_sum<G>(s, red) * (1.0f / C);
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < V; ++j)
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float d = v[j][q] - mean;
+        ss += d * d;
+      }
+    const float var = row_sum<G>(ss, red) * (1.0f / C);
+    const float inv = 1.0f / sqrtf(var + eps);
+    if (r < R && rw.g == 0) stats[r] = make_float2(mean, inv);
+  }
+}
+
 // rmsnorm: y = fp16(x * (1/sqrt(mean(x^2) + eps)) * w), w fp16
 // (kernels/rmsnorm_fp16/kernel_api.h:8-14).
 template <int G, int V>
@@ -456,6 +494,27 @@ __global__ void layernorm_f16_generic(const __half* __restrict__ x,
     for (int c = lane; c < C; c += 32)
       y[r * C + c] =
           __float2half_rn((__half2float(xr[c]) - mean) * inv * w[c] + b[c]);
+  }
+}
+
+// ln_stats for any C: one warp per row, two passes over global memory.
+__global__ void ln_stats_generic(const __half* __restrict__ x, float2* __restrict__ stats,
+                                 int64_t R, int C, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t r = warp0; r < R; r += nwarps) {
+    const __half* xr = x + r * C;
+    float s = 0.f;
+    for (int c = lane; c < C; c += 32) s += __half2float(xr[c]);
+    const float mean = warp_sum(s) / (float)C;
+    float ss = 0.f;
+    for (int c = lane; c < C; c += 32) {
+      const float d = __half2float(xr[c]) - mean;
+      ss += d * d;
+    }
+    const float var = warp_sum(ss) / (float)C;
+    if (lane == 0) stats[r] = make_float2(mean, 1.0f / sqrtf(var + eps));
   }
 }
 
@@ -921,6 +980,7 @@ int memory_kernels_init() {
   note((const void*)K<32, 2>); note((const void*)K<32, 3>); note((const void*)K<32, 4>); \
   note((const void*)K<256, 1>); note((const void*)K<256, 2>); note((const void*)K<256, 4>);
   HB_NOTE_ROWS(layernorm_rows)
+  HB_NOTE_ROWS(ln_stats_rows)
   HB_NOTE_ROWS(rmsnorm_rows)
   HB_NOTE_ROWS(softmax_rows)
 #undef HB_NOTE_ROWS
@@ -1070,6 +1130,19 @@ int launch_layernorm_f16(const void* x, const float* w, const float* b,
   HB_ROW_SWITCH(layernorm_rows, cfg, R, s, (const uint4*)x, w, b, (uint4*)y, R, eps)
   layernorm_f16_generic<<<grid_for(R * 32, kThreads), kThreads, 0, s>>>(
       (const __half*)x, w, b, (__half*)y, R, C, eps);
+  HB_LAUNCH_CHECK();
+}
+
+int launch_ln_stats_f16(const void* x, float* stats, int64_t R, int C, float eps,
+                        cudaStream_t s) {
+  if (R < 0 || C <= 0 || !x || !stats) return HEXLIB_B200_ERR_INVAL_PARAMS;
+  if (R == 0) return HEXLIB_B200_OK;
+  const bool al = aligned16(x) && (reinterpret_cast<uintptr_t>(stats) & 7u) == 0;
+  const RowCfg cfg = al ? row_cfg(C) : RowCfg{0, 0};
+  HB_ROW_SWITCH(ln_stats_rows, cfg, R, s, (const uint4*)x, (float2*)stats, R, eps)
+  if ((reinterpret_cast<uintptr_t>(stats) & 7u) != 0) return HEXLIB_B200_ERR_INVAL_PARAMS;
+  ln_stats_generic<<<grid_for(R * 32, kThreads), kThreads, 0, s>>>(
+      (const __half*)x, (float2*)stats, R, C, eps);
   HB_LAUNCH_CHECK();
 }
 

@@ -458,6 +458,88 @@ def fuse_residual(graph: Graph) -> Graph:
     return Graph(tensors, tuple(ops), graph.inputs, graph.outputs)
 
 
+def fold_layernorm(graph: Graph, derived_in: Mapping[str, tuple] | None = None
+                   ) -> tuple[Graph, dict[str, tuple]]:
+    """CUDA-only, after `fuse_qkv`: a `layernorm(x, gamma, beta)` whose only
+    consumer is a GEMM over its output with an fp16 weight W [K, N], N a
+    multiple of 256, becomes
+
+        stats = ln_stats(x)                                   [T, 2] fp32
+        out   = matmul_epilogue_ln(x, W', cols, stats)         (or ..._ln_rope)
+
+    with W' = fp16(diag(gamma) W) and cols [2, N] = (beta @ W + b; the column
+    sums of W') new consts: the GEMM's epilogue forms
+    act(rstd * (x @ W' - mean * colsum) + bias) = act(LayerNorm(x) @ W + b),
+    so the normalised rows are never written out and read back. The RoPE
+    variant takes the two segment tables interleaved ([2T, 2, 16]). New
+    consts come back as `{name: (recipe, parts, arg)}` for the batch builder."""
+    cons = _consumers(graph)
+    protected = set(graph.outputs)
+    T = graph.tensors
+    rewritten: dict[int, Op] = {}
+    new_tensors: dict[str, Tensor] = {}
+    dropped: set[str] = set()
+    derived: dict[str, tuple] = {}
+    for ln in graph.ops:
+        if ln.kind != "layernorm" or len(ln.inputs) != 3:
+            continue
+        y = ln.outputs[0]
+        users = cons.get(y, [])
+        if y in protected or len(users) != 1:
+            continue
+        mm = users[0]
+        if mm.kind not in ("matmul_epilogue", "matmul_epilogue_rope") or mm.inputs[0] != y:
+            continue
+        x, gamma, beta = ln.inputs
+        w, b = mm.inputs[1], mm.inputs[2]
+        wt, bt, xt = T[w], T[b], T[x]
+        if not (wt.const and wt.dtype == "fp16" and len(wt.shape) == 2 and bt.const and
+                bt.dtype == "fp32" and T[gamma].const and T[beta].const and
+                T[gamma].dtype == "fp32" and T[beta].dtype == "fp32"):
+            continue
+        K, N = wt.shape
+        if N % 256 or len(xt.shape) != 2 or xt.shape[1] != K or xt.dtype != "fp16":
+            continue
+        rope_src = None
+        if mm.kind == "matmul_epilogue_rope":
+            rec = (derived_in or {}).get(mm.inputs[3])
+            if rec is None or rec[0] != "rope_segments":
+                continue
+            rope_src = tuple(rec[1])
+        n_tok = xt.shape[0]
+        wf = f"lnfold_w({gamma},{w})"
+        cols = f"lnfold_cols({gamma},{beta},{w},{b})"
+        stats = f"{y}+stats"
+        new_tensors[wf] = Tensor(wf, "fp16", (K, N), True)
+        new_tensors[cols] = Tensor(cols, "fp32", (2, N), True)
+        new_tensors[stats] = Tensor(stats, "fp32", (n_tok, 2), False)
+        derived[wf] = ("ln_fold_w", (gamma, w), 0)
+        derived[cols] = ("ln_fold_cols", (gamma, beta, w, b), 0)
+        rewritten[ln.id] = Op(ln.id, "ln_stats", (x,), (stats,), {"eps": float(ln.attrs["eps"])})
+        act = {"act": mm.attrs.get("act", "none")}
+        if mm.kind == "matmul_epilogue":
+            rewritten[mm.id] = Op(mm.id, "matmul_epilogue_ln", (x, wf, cols, stats),
+                                  mm.outputs, act)
+        else:
+            seg_cos, seg_idx = mm.inputs[3], mm.inputs[5]
+            cos, sin = rope_src
+            segtab = f"rope_segtab({cos},{sin})"
+            new_tensors[segtab] = Tensor(segtab, "fp32", (T[seg_cos].shape[0], 2, 16), True)
+            derived[segtab] = ("rope_segtab", (cos, sin), 0)
+            rewritten[mm.id] = Op(mm.id, "matmul_epilogue_ln_rope",
+                                  (x, wf, cols, stats, segtab, seg_idx), mm.outputs,
+                                  dict(act, rope_cols=int(mm.attrs["rope_cols"])))
+        dropped.add(y)
+    if not rewritten:
+        return graph, {}
+    ops = tuple(rewritten.get(o.id, o) for o in graph.ops)
+    tensors = {n: t for n, t in graph.tensors.items() if n not in dropped}
+    tensors.update(new_tensors)
+    used = {n for o in ops for n in o.inputs}
+    tensors = {n: t for n, t in tensors.items() if not (t.const and n not in used)}
+    return Graph(tensors, ops, graph.inputs, graph.outputs), derived
+
+
 def fuse_qkv(graph: Graph, rope_epilogue: bool = False) -> tuple[Graph, dict[str, tuple]]:
     """CUDA-only, after `fuse_attention`: per block, the q, k and v projections
     (three matmul_epilogue over one input), their reshapes to [T, H, D], the
@@ -615,8 +697,10 @@ class ExecPlan:
     Shaped like the reference's `Compiled(graph, plan)` (compiled.py:33-66)
     where the batch builder reads it: `.graph` and `.plan.steps[i].op`.
     `derived` names consts a rewrite created, with the recipe that builds
-    each from the feeds (`("concat", parts, axis)` or
-    `("rope_segments", (cos, sin), which)`)."""
+    each from the feeds or from other derived consts (`("concat", parts,
+    axis)`, `("rope_segments", (cos, sin), which)`, `("rope_segtab", (cos,
+    sin), 0)`, `("ln_fold_w", (gamma, w), 0)`, `("ln_fold_cols", (gamma,
+    beta, w, b), 0)`)."""
     graph: Graph
     plan: "ExecSteps"
     derived: Mapping[str, tuple] = field(default_factory=dict)
@@ -629,12 +713,15 @@ class ExecSteps:
 
 
 def _apply_rewrites(g: Graph, attention: bool, residual: bool, qkv: bool,
-                    rope_epilogue: bool = False):
+                    rope_epilogue: bool = False, ln_fold: bool = False):
     derived: dict[str, tuple] = {}
     if attention or qkv:
         g = fuse_attention(g)
     if qkv:
         g, derived = fuse_qkv(g, rope_epilogue)
+    if ln_fold:
+        g, more = fold_layernorm(g, derived)
+        derived = {**derived, **more}
     if residual:
         g = fuse_residual(g)
     problems = g.problems()
@@ -644,27 +731,31 @@ def _apply_rewrites(g: Graph, attention: bool, residual: bool, qkv: bool,
 
 
 def compile_for_cuda(graph: Graph, attention: bool = False, residual: bool = False,
-                     qkv: bool = False, rope_epilogue: bool = False) -> ExecPlan:
+                     qkv: bool = False, rope_epilogue: bool = False,
+                     ln_fold: bool = False) -> ExecPlan:
     """Fuse (as the reference pipeline does), optionally apply the CUDA-only
     rewrites, and order the ops for execution (the builder's order is
     topological; every rewrite keeps it so). `qkv` implies `attention`;
-    `rope_epilogue` moves the packed path's RoPE into the qkv GEMM."""
+    `rope_epilogue` moves the packed path's RoPE into the qkv GEMM;
+    `ln_fold` folds each layernorm that feeds one GEMM into that GEMM."""
     problems = graph.problems()
     if problems:
         raise ValueError("graph is structurally invalid: " + "; ".join(problems[:5]))
-    g, derived = _apply_rewrites(fuse(graph), attention, residual, qkv, rope_epilogue)
+    g, derived = _apply_rewrites(fuse(graph), attention, residual, qkv, rope_epilogue,
+                                 ln_fold)
     return ExecPlan(g, ExecSteps(tuple(Step(o) for o in g.ops)), derived)
 
 
 def rewrite_compiled(compiled, attention: bool = False, residual: bool = False,
-                     qkv: bool = False, rope_epilogue: bool = False) -> ExecPlan:
+                     qkv: bool = False, rope_epilogue: bool = False,
+                     ln_fold: bool = False) -> ExecPlan:
     """Apply the CUDA-only rewrites to any compiled pair -- the reference's
     own `Compiled` included -- keeping its plan order for the ops that stay."""
     graph = as_graph(compiled.graph)
     order = [s.op.id for s in compiled.plan.steps if getattr(s, "op", None) is not None]
     by_id = {o.id: o for o in graph.ops}
     g = Graph(graph.tensors, tuple(by_id[i] for i in order), graph.inputs, graph.outputs)
-    g, derived = _apply_rewrites(g, attention, residual, qkv, rope_epilogue)
+    g, derived = _apply_rewrites(g, attention, residual, qkv, rope_epilogue, ln_fold)
     return ExecPlan(g, ExecSteps(tuple(Step(o) for o in g.ops)), derived)
 
 

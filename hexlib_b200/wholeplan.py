@@ -158,6 +158,71 @@ def rope_segments(cos, sin) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
     return seg_cos, seg_sin, inverse.reshape(T, 2).astype(np.int32)
 
 
+def _fp16_exact(v) -> np.ndarray:
+    """A weight as the fp16 tensor the plan would stage, in float64."""
+    return np.asarray(v, np.float32).astype(np.float16).astype(np.float64)
+
+
+def ln_fold_w(gamma, w) -> np.ndarray:
+    """diag(gamma) W rounded once to fp16: the weight a layernorm-folded GEMM
+    multiplies the raw rows by."""
+    return (np.asarray(gamma, np.float64)[:, None] * _fp16_exact(w)).astype(np.float16)
+
+
+def ln_fold_cols(gamma, beta, w, b) -> np.ndarray:
+    """[2, N] fp32: (beta @ W + b; the column sums of ln_fold_w(gamma, W)),
+    both summed in float64 and rounded once."""
+    wf = ln_fold_w(gamma, w).astype(np.float64)
+    bias = np.asarray(beta, np.float64) @ _fp16_exact(w) + np.asarray(b, np.float64)
+    return np.stack([bias, wf.sum(axis=0)]).astype(np.float32)
+
+
+class _Deriver:
+    """The value of a const: a feed, or built by its recipe from feeds and
+    other derived consts (each built once)."""
+
+    def __init__(self, derived, feeds, placements):
+        self.derived, self.feeds, self.placements = derived, feeds, placements
+        self.memo: dict[str, Any] = {}
+        self.segments: dict[tuple, tuple] = {}
+
+    def __call__(self, n: str):
+        if n in self.memo:
+            return self.memo[n]
+        if n in self.derived:
+            v = self._build(n, *self.derived[n])
+        elif n in self.feeds:
+            v = self.feeds[n]
+        else:
+            raise WholePlanError(f"no feed supplied for const {n!r}")
+        self.memo[n] = v
+        return v
+
+    def _build(self, n, how, parts, arg):
+        if how not in ("concat", "rope_segments", "rope_segtab", "ln_fold_w", "ln_fold_cols"):
+            raise WholePlanError(f"const {n!r}: unknown derivation {how!r}")
+        missing = [q for q in parts if q not in self.feeds and q not in self.derived]
+        if missing:
+            raise WholePlanError(f"const {n!r} is built from {missing}, not supplied")
+        vals = [self(q) for q in parts]
+        if how in ("rope_segments", "rope_segtab"):
+            key = tuple(parts)
+            if key not in self.segments:
+                self.segments[key] = rope_segments(vals[0], vals[1])
+            seg_cos, seg_sin, idx = self.segments[key]
+            if how == "rope_segtab":
+                return np.stack([seg_cos, seg_sin], axis=1)
+            return (seg_cos, seg_sin, idx)[arg]
+        if how == "ln_fold_w":
+            return ln_fold_w(*vals)
+        if how == "ln_fold_cols":
+            return ln_fold_cols(*vals)
+        p = self.placements.get(n)
+        if p is not None and p.dtype in quant.BLOCK_BYTES and any(_is_raw(v) for v in vals):
+            return _concat_raw(vals, p.dtype, p.shape, arg)
+        return np.concatenate([np.asarray(v) for v in vals], axis=arg)
+
+
 def build_cuda_plan(compiled, feeds: Mapping[str, Any] | None = None,
                     alias: bool = False) -> CudaPlan:
     """Pack `compiled`'s whole plan into one blob; stage `feeds`' consts if
@@ -291,30 +356,11 @@ def build_cuda_plan(compiled, feeds: Mapping[str, Any] | None = None,
     derived = dict(getattr(compiled, "derived", {}) or {})
     if feeds is not None:
         payload = bytearray(const_bytes)
-        segments: dict[tuple, tuple] = {}
+        resolve = _Deriver(derived, feeds, placements)
         for n, p in placements.items():
             if p.region != "const":
                 continue
-            if n in derived:
-                how, parts, axis = derived[n]
-                if how not in ("concat", "rope_segments"):
-                    raise WholePlanError(f"const {n!r}: unknown derivation {how!r}")
-                missing = [q for q in parts if q not in feeds]
-                if missing:
-                    raise WholePlanError(f"const {n!r} is built from {missing}, not supplied")
-                if how == "rope_segments":
-                    key = tuple(parts)
-                    if key not in segments:
-                        segments[key] = rope_segments(feeds[parts[0]], feeds[parts[1]])
-                    value = segments[key][axis]
-                elif p.dtype in quant.BLOCK_BYTES and any(_is_raw(feeds[q]) for q in parts):
-                    value = _concat_raw([feeds[q] for q in parts], p.dtype, p.shape, axis)
-                else:
-                    value = np.concatenate([np.asarray(feeds[q]) for q in parts], axis=axis)
-            elif n in feeds:
-                value = feeds[n]
-            else:
-                raise WholePlanError(f"no feed supplied for const {n!r}")
+            value = resolve(n)
             if p.dtype in quant.BLOCK_BYTES:
                 # a dense weight is quantized here, as the reference's batch
                 # builder does (wholeplan.py:293-307); packed bytes pass as is

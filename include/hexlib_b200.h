@@ -97,6 +97,9 @@ extern "C" {
 #define HEXLIB_B200_KIND_MATMUL_EPILOGUE_ROPE 16 /* act(a@w+b), RoPE on heads */
 #define HEXLIB_B200_KIND_ATTENTION_QKV    17  /* attention over packed q|k|v */
 #define HEXLIB_B200_KIND_ROPE_QK          18  /* rope_2d of the q, k sections */
+#define HEXLIB_B200_KIND_LN_STATS         19  /* layernorm's (mean, rstd) per row */
+#define HEXLIB_B200_KIND_MATMUL_EPILOGUE_LN 20 /* act(layernorm(x) @ w + b), folded */
+#define HEXLIB_B200_KIND_MATMUL_EPILOGUE_LN_ROPE 21 /* the same, RoPE on heads */
 
 /* Invoke modes. */
 #define HEXLIB_B200_MODE_GRAPH   0u  /* capture once per blob, replay one graph  */
@@ -309,6 +312,29 @@ HEXLIB_B200_API int hexlib_b200_matmul_epilogue_rope_fp16(
 HEXLIB_B200_API int hexlib_b200_rope_qk_fp16(const void *qkv, const float *costab,
                                              const float *sintab, void *out, int rows,
                                              int H, int D, int T, void *stream);
+/* layernorm (kernels/layernorm_fp16/kernel_api.h) without its output: the
+ * (mean, 1/sqrt(var + eps)) of each of R rows of C fp16, as R float pairs
+ * (stats 8-byte aligned), computed exactly as hexlib_b200_layernorm_fp16
+ * computes them. */
+HEXLIB_B200_API int hexlib_b200_ln_stats_fp16(const void *x, float *stats, int R, int C,
+                                              float eps, void *stream);
+/* act(layernorm(x) @ W + b) without materialising layernorm(x): x [M, K] raw
+ * rows, w = diag(gamma) W [K, N] fp16 (the layernorm weight folded into the
+ * matrix), cols [2, N] fp32 = (beta @ W + b; the column sums of w), stats
+ * [M, 2] from hexlib_b200_ln_stats_fp16. The epilogue forms
+ * act(rstd * (x @ w - mean * colsum) + bias). N must be a multiple of 256;
+ * act: 0 none, 1 gelu_tanh, 2 gelu_erf. */
+HEXLIB_B200_API int hexlib_b200_matmul_epilogue_ln_fp16(const void *x, const void *w,
+                                                        const float *cols, const float *stats,
+                                                        void *out, int M, int K, int N,
+                                                        int act, void *stream);
+/* The same with the RoPE epilogue of hexlib_b200_matmul_epilogue_rope_fp16;
+ * the cos and sin segment tables interleaved as one [n_seg, 2, 16] table
+ * (segment s: 16 cos values, then 16 sin values). */
+HEXLIB_B200_API int hexlib_b200_matmul_epilogue_ln_rope_fp16(
+    const void *x, const void *w, const float *cols, const float *stats, const float *segtab,
+    const int *seg_idx, int n_seg, void *out, int M, int K, int N, int act, int rope_cols,
+    int T, void *stream);
 /* Fused attention over a packed projection: qkv [B, T, 3, H, D] (the output
  * of the call above), ctx [B, T, H, D] -- the layout the o-projection reads,
  * so none of the block's four transposes is needed. D must be 64. */

@@ -122,6 +122,50 @@ def test_rope_epilogue_rewrite_moves_the_rotation_into_the_qkv_gemm():
     assert Counter(o.kind for o in q.graph.ops)["rope_qk"] == 12
 
 
+def test_layernorm_fold_rewrites_every_layernorm_that_feeds_a_gemm():
+    g = G.build_vision_encoder(G.qwen35_at(256))
+    ep = G.compile_for_cuda(g, residual=True, qkv=True, rope_epilogue=True, ln_fold=True)
+    c = Counter(o.kind for o in ep.graph.ops)
+    assert c["ln_stats"] == 24 and c["matmul_epilogue_ln_rope"] == 12
+    assert c["matmul_epilogue_ln"] == 12
+    # the merger's layernorm feeds a reshape, not a GEMM: it stays
+    assert c["layernorm"] == 1
+    assert ep.graph.problems() == []
+    for o in ep.graph.ops:
+        if o.kind == "matmul_epilogue_ln":
+            x, wf, cols, stats = o.inputs
+            t = ep.graph.tensors
+            assert t[wf].dtype == "fp16" and t[cols].shape == (2, t[wf].shape[1])
+            assert t[stats].shape == (256, 2) and not t[stats].const
+            assert ep.derived[wf][0] == "ln_fold_w" and ep.derived[cols][0] == "ln_fold_cols"
+        if o.kind == "matmul_epilogue_ln_rope":
+            segtab = ep.graph.tensors[o.inputs[4]]
+            assert segtab.shape == (512, 2, 16) and segtab.dtype == "fp32"
+    # quantized weights are not folded (the fold would requantize them)
+    q = G.compile_for_cuda(G.build_vision_encoder(G.qwen35_at(256, weight_dtype="q4_0")),
+                           residual=True, qkv=True, rope_epilogue=True, ln_fold=True)
+    assert Counter(o.kind for o in q.graph.ops)["ln_stats"] == 0
+
+
+def test_the_fold_identity_holds_in_float64():
+    """rstd (x @ W' - mean colsum(W')) + (beta @ W + b) is layernorm(x) @ W + b
+    up to the one fp16 rounding of W' = diag(gamma) W."""
+    r = np.random.default_rng(0)
+    K, N = 64, 32
+    x = (r.standard_normal((5, K)) + 4.0).astype(np.float16).astype(np.float64)
+    gamma = (1 + 0.1 * r.standard_normal(K)).astype(np.float32)
+    beta = (0.1 * r.standard_normal(K)).astype(np.float32)
+    w = (0.05 * r.standard_normal((K, N))).astype(np.float16)
+    b = (0.02 * r.standard_normal(N)).astype(np.float32)
+    mean = x.mean(1, keepdims=True)
+    rstd = 1 / np.sqrt(((x - mean) ** 2).mean(1, keepdims=True) + 1e-6)
+    exact = ((x - mean) * rstd * gamma + beta) @ w.astype(np.float64) + b
+    wf = wholeplan.ln_fold_w(gamma, w).astype(np.float64)
+    cols = wholeplan.ln_fold_cols(gamma, beta, w, b).astype(np.float64)
+    folded = rstd * (x @ wf - mean * cols[1]) + cols[0]
+    assert np.abs(folded - exact).max() < 4e-3 * np.abs(exact).max()
+
+
 def test_rope_segments_rebuild_the_tables_exactly():
     cfg = G.qwen35_at(512)
     w = F.weights(cfg, 0, G.build_vision_encoder(cfg))
