@@ -69,6 +69,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking test of a phase (never suspends). Its result is only needed
+// when it is used, so issuing it ahead of independent work (tcgen05.mma
+// instructions, say) hides the shared-memory round trip behind that work.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // The same test, but a thread whose phase is not yet complete is suspended
 // until it completes or kSuspendNs pass, instead of spinning: a waiting warp
 // then takes no issue slots from the warps that share its scheduler.
