@@ -55,6 +55,8 @@ def parse():
     ap.add_argument("--no-qkv-fusion", action="store_true")
     ap.add_argument("--rope", choices=("epilogue", "pass"), default="epilogue",
                     help="packed qkv path: RoPE in the qkv GEMM's epilogue, or its own pass")
+    ap.add_argument("--no-patch-cast", action="store_true",
+                    help="keep patchify and the cast of its rows to fp16 as two passes")
     ap.add_argument("--ln-fold", choices=("on", "off"), default="off",
                     help="fold each layernorm that feeds a GEMM into that GEMM's epilogue")
     ap.add_argument("--weights", choices=("fp16", "q4_0", "q8_0"), default="fp16",
@@ -279,7 +281,8 @@ def run_b200(args) -> None:
     use_qkv = use_att and not args.no_qkv_fusion
     ep = G.compile_for_cuda(g, attention=use_att, residual=not args.no_residual_fusion,
                             qkv=use_qkv, rope_epilogue=args.rope == "epilogue",
-                            ln_fold=args.ln_fold == "on" and args.weights == "fp16")
+                            ln_fold=args.ln_fold == "on" and args.weights == "fp16",
+                            patch_cast=not args.no_patch_cast)
     w = F.weights(cfg, 0, g)
     plan = wholeplan.build_cuda_plan(ep, w, alias=True)
     sh = D.shard(args.batch, rank, world)
@@ -439,6 +442,7 @@ def run_b200(args) -> None:
                 "weights": args.weights, "plan_ops": plan.n_ops, "fusions": {"attention": use_att, "qkv_rope": use_qkv,
                                                    "rope": args.rope if use_qkv else None,
                                                    "ln_fold": args.ln_fold == "on",
+                                                   "patch_cast": not args.no_patch_cast,
                                                    "residual": not args.no_residual_fusion},
                 "l2": f"inputs larger than L2: each step reads {plan.const_bytes / 1e6:.0f} MB "
                       f"of consts and {n * 6.29:.0f} MB of images per GPU",

@@ -83,6 +83,8 @@ _PROTOS: dict[str, list] = {
     "hexlib_b200_attention_qkv_fp16": [c_vp, c_vp, c_int, c_int, c_int, c_int, c_f, c_vp],
     "hexlib_b200_rope_qk_fp16": [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp],
     "hexlib_b200_ln_stats_fp16": [c_vp, c_vp, c_int, c_int, c_f, c_vp],
+    "hexlib_b200_patchify_fp16": [c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+                                  c_int, c_vp],
     "hexlib_b200_matmul_epilogue_ln_fp16": [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int,
                                             c_int, c_vp],
     "hexlib_b200_matmul_epilogue_ln_rope_fp16": [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int,

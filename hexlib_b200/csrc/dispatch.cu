@@ -275,10 +275,11 @@ int check_op(const OpRec& op) {
         return HEXLIB_B200_ERR_INVAL_PARAMS;
       return HEXLIB_B200_OK;
     }
-    case HEXLIB_B200_KIND_PATCHIFY: {
+    case HEXLIB_B200_KIND_PATCHIFY:
+    case HEXLIB_B200_KIND_PATCHIFY_CAST: {
       HB_TRY(need(op, 2));
       HB_TRY(dt(op, 0, DT_FP32));
-      HB_TRY(dt(op, 1, DT_FP32));
+      HB_TRY(dt(op, 1, op.kind == HEXLIB_B200_KIND_PATCHIFY ? DT_FP32 : DT_FP16));
       HB_TRY(batching(op, 1));
       const uint32_t* x = op.a[0].ne;  // C, T, H, W
       const int64_t patch = op.params[0], merge = op.params[1];
@@ -531,6 +532,11 @@ int run_op(const OpRec& op, uint32_t n_images, int* err, void* ws, uint64_t ws_b
                                      (int)a[0].ne[2], (int)a[0].ne[3],
                                      op.params[0], op.params[1], op.params[2],
                                      op.params[3], s);
+    case HEXLIB_B200_KIND_PATCHIFY_CAST:
+      return hb::launch_patchify_f32_f16((const float*)a[0].ptr, a[1].ptr, B,
+                                         (int)a[0].ne[0], (int)a[0].ne[1], (int)a[0].ne[2],
+                                         (int)a[0].ne[3], op.params[0], op.params[1],
+                                         op.params[2], op.params[3], s);
     case HEXLIB_B200_KIND_RESHAPE:
       return hb::launch_copy(a[0].ptr, a[1].ptr, (int64_t)a[0].nbytes * B, s);
     case HEXLIB_B200_KIND_MATMUL: {

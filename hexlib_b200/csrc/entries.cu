@@ -155,6 +155,13 @@ int hexlib_b200_patchify_fp32(const float* img, float* out, int C, int T,
                                  grid_w, as_stream(stream));
 }
 
+int hexlib_b200_patchify_fp16(const float* img, void* out, int C, int T, int H, int W,
+                              int patch, int merge, int grid_h, int grid_w, void* stream) {
+  HB_ENTRY_INIT();
+  return hb::launch_patchify_f32_f16(img, out, 1, C, T, H, W, patch, merge, grid_h, grid_w,
+                                     as_stream(stream));
+}
+
 int hexlib_b200_matmul_fp16(const void* A, const void* B, void* C, int Bn,
                             int M, int K, int N, void* stream) {
   HB_ENTRY_INIT();

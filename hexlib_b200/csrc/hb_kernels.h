@@ -30,6 +30,10 @@ int launch_copy(const void* x, void* y, int64_t nbytes, cudaStream_t s);
 // Row-wise.
 int launch_layernorm_f16(const void* x, const float* w, const float* b,
                          void* y, int64_t R, int C, float eps, cudaStream_t s);
+// patchify with its output rounded to fp16 (patchify then cast, in one pass).
+int launch_patchify_f32_f16(const float* img, void* out, int64_t nimg, int C, int T, int H,
+                            int W, int patch, int merge, int grid_h, int grid_w,
+                            cudaStream_t s);
 // (mean, 1/sqrt(var + eps)) of each of R rows of C fp16, as float2 pairs.
 int launch_ln_stats_f16(const void* x, float* stats, int64_t R, int C, float eps,
                         cudaStream_t s);

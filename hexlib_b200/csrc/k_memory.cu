@@ -868,7 +868,11 @@ __global__ void patchify_vec(const float4* __restrict__ img,
 // tabulates, for each output float4 of a token, its source offset from the
 // patch's top-left corner -- so the copy loop has no divisions, which
 // otherwise cost more issue slots than the move itself.
-__global__ void patchify_blocks(const float4* __restrict__ img, float4* __restrict__ out,
+// OUT_F16: each float4 is rounded to four fp16 on the way out (round to
+// nearest even, as the cast op rounds), so patchify followed by the cast to
+// fp16 becomes one pass that writes half the bytes.
+template <bool OUT_F16>
+__global__ void patchify_blocks(const float4* __restrict__ img, void* __restrict__ out,
                                 int64_t n_blocks, int blocks_per_img, int bw_n, int merge,
                                 int patch, int C, int T, int H, int W4, int fv) {
   extern __shared__ int src_off[];             // [fv]
@@ -890,14 +894,26 @@ __global__ void patchify_blocks(const float4* __restrict__ img, float4* __restri
     const int rb = (int)(mb - n * blocks_per_img);
     const int bh = rb / bw_n, bw = rb - bh * bw_n;
     const float4* src_n = img + n * img4;
-    float4* dst = out + mb * mm * (int64_t)fv;
+    const int64_t dst0 = mb * mm * (int64_t)fv;     // in float4 units of the output
     for (int m = 0; m < mm; ++m) {
       const int mh = m / merge, mw = m - mh * merge;
       const float4* src =
           src_n + (int64_t)((bh * merge + mh) * patch) * W4 + (bw * merge + mw) * pv;
-      float4* d = dst + (int64_t)m * fv;
+      const int64_t d0 = dst0 + (int64_t)m * fv;
+      if constexpr (OUT_F16) {
+        uint2* d = reinterpret_cast<uint2*>(out) + d0;
 #pragma unroll 4
-      for (int f = threadIdx.x; f < fv; f += blockDim.x) d[f] = __ldg(src + src_off[f]);
+        for (int f = threadIdx.x; f < fv; f += blockDim.x) {
+          const float4 v = __ldg(src + src_off[f]);
+          const __half2 lo = __floats2half2_rn(v.x, v.y), hi = __floats2half2_rn(v.z, v.w);
+          d[f] = make_uint2(*reinterpret_cast<const uint32_t*>(&lo),
+                            *reinterpret_cast<const uint32_t*>(&hi));
+        }
+      } else {
+        float4* d = reinterpret_cast<float4*>(out) + d0;
+#pragma unroll 4
+        for (int f = threadIdx.x; f < fv; f += blockDim.x) d[f] = __ldg(src + src_off[f]);
+      }
     }
   }
 }
@@ -1133,6 +1149,29 @@ int launch_layernorm_f16(const void* x, const float* w, const float* b,
   HB_LAUNCH_CHECK();
 }
 
+int launch_patchify_f32_f16(const float* img, void* out, int64_t nimg, int C, int T, int H,
+                            int W, int patch, int merge, int grid_h, int grid_w,
+                            cudaStream_t s) {
+  if (nimg < 0 || C <= 0 || T <= 0 || patch <= 0 || merge <= 0 || grid_h <= 0 ||
+      grid_w <= 0 || grid_h * patch != H || grid_w * patch != W || grid_h % merge ||
+      grid_w % merge || !img || !out)
+    return HEXLIB_B200_ERR_INVAL_PARAMS;
+  if (nimg == 0) return HEXLIB_B200_OK;
+  const int fv = C * T * patch * patch / 4;
+  // the merge-block kernel only: 16-byte image rows, 8-byte output runs
+  if ((patch % 4) || !aligned16(img) || (reinterpret_cast<uintptr_t>(out) & 7u) ||
+      fv > 8192 || (int64_t)C * T * H * W >= ((int64_t)1 << 31))
+    return HEXLIB_B200_ERR_INVAL_PARAMS;
+  const int bw_n = grid_w / merge;
+  const int per_img = (grid_h / merge) * bw_n;
+  const int64_t n_blocks = nimg * per_img;
+  const int64_t cap = (int64_t)sm_count_cached() * 16;
+  patchify_blocks<true><<<(unsigned)(n_blocks < cap ? n_blocks : cap), 128,
+                          (size_t)fv * sizeof(int), s>>>(
+      (const float4*)img, out, n_blocks, per_img, bw_n, merge, patch, C, T, H, W / 4, fv);
+  HB_LAUNCH_CHECK();
+}
+
 int launch_ln_stats_f16(const void* x, float* stats, int64_t R, int C, float eps,
                         cudaStream_t s) {
   if (R < 0 || C <= 0 || !x || !stats) return HEXLIB_B200_ERR_INVAL_PARAMS;
@@ -1254,10 +1293,9 @@ int launch_patchify_f32(const float* img, float* out, int64_t nimg, int C,
     const int per_img = (grid_h / merge) * bw_n;
     const int64_t n_blocks = nimg * per_img;
     const int64_t cap = (int64_t)sm_count_cached() * 16;
-    patchify_blocks<<<(unsigned)(n_blocks < cap ? n_blocks : cap), 128,
-                      (size_t)fv * sizeof(int), s>>>(
-        (const float4*)img, (float4*)out, n_blocks, per_img, bw_n, merge, patch, C, T, H,
-        W / 4, fv);
+    patchify_blocks<false><<<(unsigned)(n_blocks < cap ? n_blocks : cap), 128,
+                             (size_t)fv * sizeof(int), s>>>(
+        (const float4*)img, out, n_blocks, per_img, bw_n, merge, patch, C, T, H, W / 4, fv);
   } else if ((patch % 4) == 0 && aligned16(img) && aligned16(out)) {
     patchify_vec<<<grid_for(total / 4, kThreads), kThreads, 0, s>>>(
         (const float4*)img, (float4*)out, nimg, C, T, H, W, patch, merge,

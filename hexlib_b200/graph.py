@@ -458,6 +458,37 @@ def fuse_residual(graph: Graph) -> Graph:
     return Graph(tensors, tuple(ops), graph.inputs, graph.outputs)
 
 
+def fuse_patchify_cast(graph: Graph) -> Graph:
+    """CUDA-only: `cast(patchify(image), fp16)` whose fp32 patch rows have no
+    other consumer becomes one `patchify_cast(image)` writing the fp16 rows
+    (each value rounded to nearest even, as the cast rounds it): one pass
+    over the image instead of a write and a re-read of the fp32 rows."""
+    cons = _consumers(graph)
+    protected = set(graph.outputs)
+    T = graph.tensors
+    rewritten: dict[int, Op] = {}
+    consumed: set[int] = set()
+    dropped: set[str] = set()
+    for pt in graph.ops:
+        if pt.kind != "patchify":
+            continue
+        rows = pt.outputs[0]
+        users = cons.get(rows, [])
+        if rows in protected or len(users) != 1:
+            continue
+        cast = users[0]
+        if cast.kind != "cast" or cast.attrs.get("dtype") != "fp16" or T[rows].dtype != "fp32":
+            continue
+        rewritten[pt.id] = Op(pt.id, "patchify_cast", pt.inputs, cast.outputs, dict(pt.attrs))
+        consumed.add(cast.id)
+        dropped.add(rows)
+    if not rewritten:
+        return graph
+    ops = tuple(rewritten.get(o.id, o) for o in graph.ops if o.id not in consumed)
+    tensors = {n: t for n, t in graph.tensors.items() if n not in dropped}
+    return Graph(tensors, ops, graph.inputs, graph.outputs)
+
+
 def fold_layernorm(graph: Graph, derived_in: Mapping[str, tuple] | None = None
                    ) -> tuple[Graph, dict[str, tuple]]:
     """CUDA-only, after `fuse_qkv`: a `layernorm(x, gamma, beta)` whose only
@@ -713,8 +744,11 @@ class ExecSteps:
 
 
 def _apply_rewrites(g: Graph, attention: bool, residual: bool, qkv: bool,
-                    rope_epilogue: bool = False, ln_fold: bool = False):
+                    rope_epilogue: bool = False, ln_fold: bool = False,
+                    patch_cast: bool = False):
     derived: dict[str, tuple] = {}
+    if patch_cast:
+        g = fuse_patchify_cast(g)
     if attention or qkv:
         g = fuse_attention(g)
     if qkv:
@@ -732,30 +766,32 @@ def _apply_rewrites(g: Graph, attention: bool, residual: bool, qkv: bool,
 
 def compile_for_cuda(graph: Graph, attention: bool = False, residual: bool = False,
                      qkv: bool = False, rope_epilogue: bool = False,
-                     ln_fold: bool = False) -> ExecPlan:
+                     ln_fold: bool = False, patch_cast: bool = False) -> ExecPlan:
     """Fuse (as the reference pipeline does), optionally apply the CUDA-only
     rewrites, and order the ops for execution (the builder's order is
     topological; every rewrite keeps it so). `qkv` implies `attention`;
     `rope_epilogue` moves the packed path's RoPE into the qkv GEMM;
-    `ln_fold` folds each layernorm that feeds one GEMM into that GEMM."""
+    `ln_fold` folds each layernorm that feeds one GEMM into that GEMM;
+    `patch_cast` writes the patch rows as fp16 straight from patchify."""
     problems = graph.problems()
     if problems:
         raise ValueError("graph is structurally invalid: " + "; ".join(problems[:5]))
     g, derived = _apply_rewrites(fuse(graph), attention, residual, qkv, rope_epilogue,
-                                 ln_fold)
+                                 ln_fold, patch_cast)
     return ExecPlan(g, ExecSteps(tuple(Step(o) for o in g.ops)), derived)
 
 
 def rewrite_compiled(compiled, attention: bool = False, residual: bool = False,
                      qkv: bool = False, rope_epilogue: bool = False,
-                     ln_fold: bool = False) -> ExecPlan:
+                     ln_fold: bool = False, patch_cast: bool = False) -> ExecPlan:
     """Apply the CUDA-only rewrites to any compiled pair -- the reference's
     own `Compiled` included -- keeping its plan order for the ops that stay."""
     graph = as_graph(compiled.graph)
     order = [s.op.id for s in compiled.plan.steps if getattr(s, "op", None) is not None]
     by_id = {o.id: o for o in graph.ops}
     g = Graph(graph.tensors, tuple(by_id[i] for i in order), graph.inputs, graph.outputs)
-    g, derived = _apply_rewrites(g, attention, residual, qkv, rope_epilogue, ln_fold)
+    g, derived = _apply_rewrites(g, attention, residual, qkv, rope_epilogue, ln_fold,
+                                 patch_cast)
     return ExecPlan(g, ExecSteps(tuple(Step(o) for o in g.ops)), derived)
 
 

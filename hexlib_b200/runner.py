@@ -20,8 +20,8 @@ DIFFERENCES FROM THE DSP's TABLE, each deliberate:
     reshapes by aliasing, but a blob that carries one is served.
   * ids are appended for kernels the DSP table does not have: attention (13),
     rmsnorm (14), matmul_epilogue_residual (15), matmul_epilogue_rope (16),
-    attention_qkv (17), rope_qk (18), ln_stats (19), matmul_epilogue_ln (20)
-    and matmul_epilogue_ln_rope (21).
+    attention_qkv (17), rope_qk (18), ln_stats (19), matmul_epilogue_ln (20),
+    matmul_epilogue_ln_rope (21) and patchify_cast (22).
 """
 from __future__ import annotations
 
@@ -52,6 +52,7 @@ KIND_ID: dict[str, int] = {
     "ln_stats": 19,
     "matmul_epilogue_ln": 20,
     "matmul_epilogue_ln_rope": 21,
+    "patchify_cast": 22,
 }
 
 ACT_CODES = (("none", 0), ("gelu_tanh", 1), ("gelu_erf", 2))
@@ -157,6 +158,10 @@ SPECS: dict[str, CudaSpec] = {
         params=(Param("act", "int", ACT_CODES), Param("rope_cols")),
         entry="hexlib_b200_matmul_epilogue_rope_fp16"),
     "rope_qk": CudaSpec("rope_qk", (F16, F32, F32), "fp16", entry="hexlib_b200_rope_qk_fp16"),
+    "patchify_cast": CudaSpec("patchify_cast", (F32,), "fp16",
+                              params=(Param("patch"), Param("merge"), Param("grid_h"),
+                                      Param("grid_w")),
+                              entry="hexlib_b200_patchify_fp16"),
     "ln_stats": CudaSpec("ln_stats", (F16,), "fp32", params=(Param("eps", "float"),),
                          entry="hexlib_b200_ln_stats_fp16"),
     "matmul_epilogue_ln": CudaSpec(

@@ -100,6 +100,7 @@ extern "C" {
 #define HEXLIB_B200_KIND_LN_STATS         19  /* layernorm's (mean, rstd) per row */
 #define HEXLIB_B200_KIND_MATMUL_EPILOGUE_LN 20 /* act(layernorm(x) @ w + b), folded */
 #define HEXLIB_B200_KIND_MATMUL_EPILOGUE_LN_ROPE 21 /* the same, RoPE on heads */
+#define HEXLIB_B200_KIND_PATCHIFY_CAST    22  /* patchify, then cast to fp16 */
 
 /* Invoke modes. */
 #define HEXLIB_B200_MODE_GRAPH   0u  /* capture once per blob, replay one graph  */
@@ -236,6 +237,13 @@ HEXLIB_B200_API int hexlib_b200_transpose_hd_fp16(const void *x, void *y, int B,
 HEXLIB_B200_API int hexlib_b200_patchify_fp32(const float *img, float *out, int C, int T,
                               int H, int W, int patch, int merge, int grid_h,
                               int grid_w, void *stream);
+/* patchify followed by the cast of its rows to fp16, in one pass: the
+ * arguments of hexlib_b200_patchify_fp32, an fp16 output (8-byte aligned);
+ * each value rounded to nearest even exactly as the cast rounds it. patch
+ * must be a multiple of 4 and img 16-byte aligned. */
+HEXLIB_B200_API int hexlib_b200_patchify_fp16(const float *img, void *out, int C, int T,
+                                              int H, int W, int patch, int merge,
+                                              int grid_h, int grid_w, void *stream);
 /* kernels/matmul_fp16/kernel_api.h:77-78 */
 HEXLIB_B200_API int hexlib_b200_matmul_fp16(const void *A, const void *B, void *C, int Bn,
                             int M, int K, int N, void *stream);

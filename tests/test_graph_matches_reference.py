@@ -147,6 +147,16 @@ def test_layernorm_fold_rewrites_every_layernorm_that_feeds_a_gemm():
     assert Counter(o.kind for o in q.graph.ops)["ln_stats"] == 0
 
 
+def test_patchify_cast_rewrite_replaces_the_pair():
+    g = G.build_vision_encoder(G.qwen35_at(256))
+    ep = G.compile_for_cuda(g, residual=True, patch_cast=True)
+    c = Counter(o.kind for o in ep.graph.ops)
+    assert c["patchify_cast"] == 1 and c["patchify"] == 0 and c["cast"] == 0
+    op = next(o for o in ep.graph.ops if o.kind == "patchify_cast")
+    assert ep.graph.tensors[op.outputs[0]].dtype == "fp16"
+    assert ep.graph.problems() == []
+
+
 def test_the_fold_identity_holds_in_float64():
     """rstd (x @ W' - mean colsum(W')) + (beta @ W + b) is layernorm(x) @ W + b
     up to the one fp16 rounding of W' = diag(gamma) W."""

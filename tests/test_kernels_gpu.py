@@ -202,6 +202,18 @@ def test_patchify_is_bit_exact(S, p, m):
     assert_bit_exact(G.host(y), want, "patchify")
 
 
+@pytest.mark.parametrize("S,p,m", [(512, 16, 2), (256, 16, 2), (64, 8, 2), (96, 4, 3)])
+def test_patchify_to_fp16_is_patchify_then_cast_bit_for_bit(S, p, m):
+    img = (rng(21).standard_normal((3, 2, S, S)) * 3).astype(np.float32)
+    g = S // p
+    attrs = {"patch": p, "temporal_patch": 2, "merge": m, "grid_h": g, "grid_w": g}
+    want = ops.patchify((img,), attrs)[0].astype(np.float16)   # the cast op: nearest even
+    y = G.empty(want.shape, np.float16)
+    di = G.dev(img)
+    G.call("hexlib_b200_patchify_fp16", G.ptr(di), G.ptr(y), 3, 2, S, S, p, m, g, g, G.stream())
+    assert_bit_exact(G.host(y), want, "patchify -> fp16")
+
+
 def test_patchify_matches_the_registrys_reshape_chain():
     # The oracle's scalar index map against the reference's own reshape /
     # transpose(2,5,3,6,0,1,4,7) formulation (structural.py:200-207).

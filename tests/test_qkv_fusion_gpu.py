@@ -115,16 +115,18 @@ def test_packed_attention_refuses_what_it_cannot_serve():
     assert U.call_rc("hexlib_b200_attention_qkv_fp16", 0, 0, 1, 64, 2, 64, -1.0, 0) == 6
 
 
-@pytest.mark.parametrize("rope_epilogue", [False, True])
-def test_fully_fused_encoder_matches_the_oracle(rope_epilogue):
+@pytest.mark.parametrize("rope_epilogue,patch_cast", [(False, False), (True, True)])
+def test_fully_fused_encoder_matches_the_oracle(rope_epilogue, patch_cast):
     cfg = G.qwen35_at(256)
     g = G.build_vision_encoder(cfg)
     w = F.weights(cfg, 0, g)
     imgs = F.images(cfg, 2, 21)
-    ep = G.compile_for_cuda(g, residual=True, qkv=True, rope_epilogue=rope_epilogue)
+    ep = G.compile_for_cuda(g, residual=True, qkv=True, rope_epilogue=rope_epilogue,
+                            patch_cast=patch_cast)
     plan = wholeplan.build_cuda_plan(ep, w, alias=True)
     assert plan.kinds.count("attention_qkv") == 12
     assert plan.kinds.count("matmul_epilogue_rope") == (12 if rope_epilogue else 0)
+    assert plan.kinds.count("patchify_cast") == (1 if patch_cast else 0)
     with Session(0) as s:
         s.load(plan, max_images=2)
         out = s.run(np.ascontiguousarray(imgs))
