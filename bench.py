@@ -61,6 +61,10 @@ def parse():
                     help="fold each layernorm that feeds a GEMM into that GEMM's epilogue")
     ap.add_argument("--weights", choices=("fp16", "q4_0", "q8_0"), default="fp16",
                     help="matmul weight dtype (q4_0 is the reference model's own)")
+    ap.add_argument("--gates", action="store_true",
+                    help="instead of the encoder: the configuration-2 kernel gates (one GPU), "
+                         "each with the reference's compiled baseline.c and the numpy "
+                         "oracle timed on this host as the CPU baseline")
     ap.add_argument("--sweep", action="store_true",
                     help="instead of the encoder: the memory-bound kernel sweep (one GPU), "
                          "one JSON line per kernel and shape")
@@ -487,9 +491,133 @@ def run_sweep(args) -> None:
         print(json.dumps(row), flush=True)
 
 
+def _gate_cpu(case):
+    """CPU baselines of one gate: the reference's own scalar kernel
+    (kernels/<kernel>/baseline.c, compiled into oracle/_ref; one core) and the
+    numpy restatement (oracle/ops.py), median seconds of 5 (or 3) runs. The
+    matmul_epilogue baseline.c takes q4_0 weights only (its signature in
+    kernel_api.h), so it is timed with the weight quantized."""
+    import ctypes
+    import time
+
+    import numpy as np
+
+    from hexlib_b200 import quant
+    from oracle import cref, ops
+    r = np.random.default_rng(1)
+    R, C, k = case.rows, case.width, case.kind
+    F = ctypes.c_float
+
+    def f16(*shape):
+        return r.standard_normal(shape).astype(np.float16)
+
+    ref, numpy_fn = None, None
+    if k == "matmul_epilogue":
+        M, N, K = R, C, case.depth
+        a, w = f16(M, K), (0.02 * r.standard_normal((K, N))).astype(np.float32)
+        b = (0.02 * r.standard_normal(N)).astype(np.float32)
+        raw = np.frombuffer(quant.quantize_q4_0(w), np.uint8).copy()
+        y = np.empty((M, N), np.float16)
+        ref = lambda: cref.call("matmul_epilogue_fp16", a, raw, b, y, M, K, N, 1)  # noqa: E731
+        numpy_fn = lambda: ops.matmul_epilogue(  # noqa: E731
+            (a.astype(np.float32), w.astype(np.float16).astype(np.float32), b),
+            {"act": "gelu_tanh"})
+    elif k in ("softmax", "layernorm", "rmsnorm", "add", "scale"):
+        x, y = f16(R, C), np.empty((R, C), np.float16)
+        if k == "softmax":
+            ref = lambda: cref.call("softmax_fp16", x, y, R, C)  # noqa: E731
+            numpy_fn = lambda: ops.softmax((x,), {"axis": -1})  # noqa: E731
+        elif k == "layernorm":
+            w1 = (1 + 0.02 * r.standard_normal(C)).astype(np.float32)
+            b1 = (0.02 * r.standard_normal(C)).astype(np.float32)
+            ref = lambda: cref.call("layernorm_fp16", x, w1, b1, y, R, C, F(1e-6))  # noqa: E731
+            numpy_fn = lambda: ops.layernorm((x, w1, b1), {"eps": 1e-6})  # noqa: E731
+        elif k == "rmsnorm":
+            g1 = f16(C)
+            ref = lambda: cref.call("rmsnorm_fp16", x, g1, y, R, C, F(1e-6))  # noqa: E731
+            numpy_fn = lambda: ops.rmsnorm((x, g1), {"eps": 1e-6})  # noqa: E731
+        elif k == "add":
+            x2 = f16(R, C)
+            ref = lambda: cref.call("add_fp16", x, x2, y, R * C)  # noqa: E731
+            numpy_fn = lambda: ops.add((x, x2), {})  # noqa: E731
+        else:
+            ref = lambda: cref.call("scale_fp16", x, y, R * C, F(0.125))  # noqa: E731
+            numpy_fn = lambda: ops.scale((x,), {"factor": 0.125})  # noqa: E731
+    elif k == "cast":
+        x, y = r.standard_normal((R, C)).astype(np.float32), np.empty((R, C), np.float16)
+        ref = lambda: cref.call("cast_f32_f16", x, y, R * C)  # noqa: E731
+        numpy_fn = lambda: ops.cast((x,), {"dtype": "fp16"})  # noqa: E731
+    elif k in ("rope_2d", "transpose_th", "transpose_hd"):
+        H, D = case.heads, 64
+        if k == "rope_2d":
+            x, y = f16(R, H, D), np.empty((R, H, D), np.float16)
+            ang = r.uniform(0, 6.283, (R, D)).astype(np.float32)
+            cs, sn = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+            ref = lambda: cref.call("rope_2d_fp16", x, cs, sn, y, R, H, D)  # noqa: E731
+            numpy_fn = lambda: ops.rope_2d((x, cs, sn), {})  # noqa: E731
+        elif k == "transpose_th":
+            x, y = f16(R, H, D), np.empty((H, R, D), np.float16)
+            ref = lambda: cref.call("transpose_th_fp16", x, y, R, H, D)  # noqa: E731
+            numpy_fn = lambda: np.ascontiguousarray(  # noqa: E731
+                ops.transpose((x,), {"perm": (1, 0, 2)})[0])
+        else:
+            x, y = f16(H, R, D), np.empty((H, D, R), np.float16)
+            ref = lambda: cref.call("transpose_hd_fp16", x, y, H, R, D)  # noqa: E731
+            numpy_fn = lambda: np.ascontiguousarray(  # noqa: E731
+                ops.transpose((x,), {"perm": (0, 2, 1)})[0])
+
+    def med(fn):
+        # median of 5 runs (of 3 when one run takes over half a second)
+        ts = []
+        for i in range(5):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+            if i == 2 and min(ts) > 0.5:
+                break
+        return sorted(ts)[len(ts) // 2]
+
+    out = {}
+    if ref is not None and cref.available():
+        out["baseline_c_us"] = round(med(ref) * 1e6, 1)
+    if numpy_fn is not None:
+        out["numpy_oracle_us"] = round(med(numpy_fn) * 1e6, 1)
+    return out
+
+
+def run_gates(args) -> None:
+    """The configuration-2 kernel gates on this rank's GPU (rank 0 prints)."""
+    import torch
+
+    from hexlib_b200 import dist as D
+    from hexlib_b200 import sweep
+    rank, local, _ = D.env_rank()
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    pk = peaks()
+    for cs in sweep.GATES:
+        t = sweep.time_case(cs, reps=20)
+        row = {"gate": cs.kind, "shape": cs.label(), "us": round(t * 1e6, 2)}
+        if cs.flops:
+            tf = cs.flops / t / 1e12
+            row.update({"bound": "tensor", "achieved": round(tf, 1), "unit": "TFLOP/s",
+                        "peak": pk["tc"], "frac": round(tf / pk["tc"], 4)})
+        else:
+            gbs = cs.bytes / t / 1e9
+            row.update({"bound": "hbm", "achieved": round(gbs, 1), "unit": "GB/s",
+                        "peak": pk["hbm"], "frac": round(gbs / pk["hbm"], 4)})
+        row["peak_source"] = pk["src"]
+        row["cpu_baseline"] = dict(_gate_cpu(cs), cores=1,
+                                   kind="reference baseline.c and the numpy port")
+        print(json.dumps(row), flush=True)
+
+
 def main():
     args = parse()
-    if args.sweep:
+    if args.gates:
+        run_gates(args)
+    elif args.sweep:
         run_sweep(args)
     elif args.impl == "reference":
         run_reference(args)
