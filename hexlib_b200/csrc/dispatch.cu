@@ -20,6 +20,7 @@
 // carry nanoseconds of device time measured with CUDA events.
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <map>
@@ -30,6 +31,28 @@
 
 #include "../../include/hexlib_b200.h"
 #include "hb_kernels.h"
+
+namespace hb {
+namespace {
+thread_local int t_walk = 0;
+bool walk_alternates() {
+  static const bool alt = [] {
+    const char* e = getenv("HEXLIB_B200_WALK_ORDER");
+    return !(e && strcmp(e, "ascending") == 0);
+  }();
+  return alt;
+}
+}  // namespace
+
+int order_next() {
+  if (!walk_alternates()) return 0;
+  const int o = t_walk;
+  t_walk ^= 1;
+  return o;
+}
+
+void order_reset() { t_walk = 0; }
+}  // namespace hb
 
 namespace {
 
@@ -892,6 +915,7 @@ int run_eager(hexlib_b200_ctx* ctx, const Parsed& p, uint32_t n,
   }
   cudaEventRecord(ctx->ev0, ctx->stream);
   if (timed && n) cudaEventRecord(ctx->op_events[0], ctx->stream);
+  hb::order_reset();
   for (uint32_t i = 0; i < n; ++i) {
     const int rc = run_op(p.ops[i], n_images, ctx->err_dev, ctx->ws, ctx->ws_bytes,
                           ctx->stream);
@@ -1311,6 +1335,7 @@ int hexlib_b200_invoke_images(hexlib_b200_ctx* ctx, const uint8_t* batch,
       write_rsp_hdr(rsp, HEXLIB_B200_ERR_CUDA, 0, 0);
       return HEXLIB_B200_ERR_CUDA;
     }
+    hb::order_reset();
     for (uint32_t i = 0; i < n_ok; ++i) {
       launch_rc = run_op(p.ops[i], n_images, ctx->err_dev, ctx->ws, ctx->ws_bytes,
                          ctx->stream);

@@ -15,6 +15,18 @@
 
 namespace hb {
 
+// Walk order of the persistent kernels (GEMM tiles, attention items,
+// layernorm rows). Consecutive launches on a host thread alternate between
+// ascending and descending order, so that a kernel first reads the rows its
+// producer wrote last -- the ones still in L2. Every tile, item and row is
+// computed the same way in either order; only the schedule changes.
+// order_next() returns 0 (ascending) or 1 (descending) and flips the
+// thread's state; order_reset() restarts it at ascending (the dispatcher
+// does so before each batch, so a captured plan is the same every time).
+// HEXLIB_B200_WALK_ORDER=ascending fixes every launch at ascending.
+int order_next();
+void order_reset();
+
 // Elementwise. `nb` is the right operand's element count: it is broadcast
 // with period nb (nb == n for a plain add; nb < n when a per-image tensor is
 // added to one shared by every image).
@@ -99,6 +111,8 @@ struct GemmDesc {
   // when bias = beta @ W + the original bias.
   const float* ln_stats = nullptr;
   const float* ln_colsum = nullptr;
+  // tile walk order, set by launch_gemm from order_next()
+  int reverse = 0;
 };
 int launch_gemm(const GemmDesc& g, int* err, cudaStream_t s);
 

@@ -61,6 +61,7 @@ struct AttnParams {
   float c_log2;       // scale * log2(e)
   __half* out;        // row (b, t) of head h at ((b*T + t)*H + h)*64
   int* err;
+  int reverse;        // walk the items last to first (the order only)
 };
 
 // 2^x with the hardware's approximate exponential (one MUFU.EX2): the
@@ -139,8 +140,9 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  // Work item w (this CTA takes w = blockIdx.x, + gridDim.x, ...): the
-  // query pair w % q_pairs of head (w / q_pairs) % H of image w / q_pairs / H.
+  // Work item w (this CTA takes w = blockIdx.x, + gridDim.x, ...): with
+  // wi = w (or items - 1 - w when p.reverse), the query pair wi % q_pairs of
+  // head (wi / q_pairs) % H of image wi / q_pairs / H.
   // Every barrier phase runs on across items: the i-th item of this CTA uses
   // Q buffer i & 1 and key blocks g = i*nkv .. i*nkv + nkv - 1 of the CTA's
   // stream.
@@ -149,9 +151,10 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       uint32_t g = 0;
       int64_t i = 0;
       for (int64_t w = blockIdx.x; w < items; w += gridDim.x, ++i) {
-        const int64_t bh = w / p.q_pairs;
+        const int64_t wi = p.reverse ? items - 1 - w : w;
+        const int64_t bh = wi / p.q_pairs;
         const int bimg = (int)(bh / p.H), head = (int)(bh % p.H);
-        const int q0 = (int)(w % p.q_pairs) * (2 * AT_BM);
+        const int q0 = (int)(wi % p.q_pairs) * (2 * AT_BM);
         const int qb = (int)(i & 1);
         // the buffer's previous item (i - 2) has finished its S products
         if (!mbar_wait(&q_empty[qb], ((uint32_t)(i >> 1) & 1u) ^ 1u, abort_flag, p.err))
@@ -247,9 +250,10 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     uint32_t g0 = 0;
     int64_t i = 0;
     for (int64_t w = blockIdx.x; w < items; w += gridDim.x, ++i, g0 += nkv) {
-      const int64_t bh = w / p.q_pairs;
+      const int64_t wi = p.reverse ? items - 1 - w : w;
+      const int64_t bh = wi / p.q_pairs;
       const int bimg = (int)(bh / p.H), head = (int)(bh % p.H);
-      const int q0 = (int)(w % p.q_pairs) * (2 * AT_BM);
+      const int q0 = (int)(wi % p.q_pairs) * (2 * AT_BM);
       float m_run = -INFINITY, l_run = 0.f;
       for (int j = 0; j < nkv; ++j) {
         const uint32_t g = g0 + (uint32_t)j;
@@ -469,6 +473,7 @@ int launch_attention(const void* q, const void* k, const void* v, void* ctx, int
       p.c_log2 = scale * 1.4426950408889634f;
       p.out = reinterpret_cast<__half*>(ctx);
       p.err = err;
+      p.reverse = order_next();
       attention_tc<<<persistent_grid(Bn * p.q_pairs), AT_THREADS, AT_SMEM, s>>>(mq, mk, mv, p);
       if (cudaPeekAtLastError() != cudaSuccess) {
         cudaGetLastError();
@@ -516,6 +521,7 @@ int launch_attention_qkv(const void* qkv, void* ctx, int64_t B, int T, int H, in
   p.c_log2 = scale * 1.4426950408889634f;
   p.out = reinterpret_cast<__half*>(ctx);
   p.err = err;
+  p.reverse = order_next();
   attention_tc<<<persistent_grid(p.Bn * p.q_pairs), AT_THREADS, AT_SMEM, s>>>(m, m, m, p);
   if (cudaPeekAtLastError() != cudaSuccess) {
     cudaGetLastError();

@@ -86,6 +86,9 @@ struct GemmParams {
   // the value is rstd * (acc - mean * colsum) + bias.
   const float* ln_stats;
   const float* ln_colsum;
+  // walk the tiles last to first: tile t of the loop is tile total_tiles-1-t
+  // (the order only; every tile is computed the same way)
+  int reverse;
 };
 
 // One whole 32-byte sector per thread (sm_100's 256-bit load): a residual
@@ -395,8 +398,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       for (int64_t t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
-        const int64_t b = t / tiles_per_batch;
-        const int64_t r = t - b * tiles_per_batch;
+        const int64_t tt = p.reverse ? p.total_tiles - 1 - t : t;
+        const int64_t b = tt / tiles_per_batch;
+        const int64_t r = tt - b * tiles_per_batch;
         const int mb = (int)(r / p.tiles_n);
         const int nb = (int)(r % p.tiles_n);
         const int bz = p.b_shared ? 0 : (int)b;
@@ -468,8 +472,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int64_t t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
-      const int64_t b = t / tiles_per_batch;
-      const int64_t r = t - b * tiles_per_batch;
+      const int64_t tt = p.reverse ? p.total_tiles - 1 - t : t;
+      const int64_t b = tt / tiles_per_batch;
+      const int64_t r = tt - b * tiles_per_batch;
       const int mb = (int)(r / p.tiles_n);
       const int nb = (int)(r % p.tiles_n);
       // Every lane waits; the warp proceeds only if all of them saw the
@@ -610,8 +615,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       for (int64_t t = pair_id; t < p.total_tiles; t += n_pairs) {
-        const int64_t b = t / tiles_per_batch;
-        const int64_t r = t - b * tiles_per_batch;
+        const int64_t tt = p.reverse ? p.total_tiles - 1 - t : t;
+        const int64_t b = tt / tiles_per_batch;
+        const int64_t r = tt - b * tiles_per_batch;
         const int mb = (int)(r / p.tiles_n);
         const int nb = (int)(r % p.tiles_n);
         const int bz = p.b_shared ? 0 : (int)b;
@@ -687,8 +693,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint32_t acc_phase = 0;
     uint32_t r_phase = 0;
     for (int64_t t = pair_id; t < p.total_tiles; t += n_pairs) {
-      const int64_t b = t / tiles_per_batch;
-      const int64_t r = t - b * tiles_per_batch;
+      const int64_t tt = p.reverse ? p.total_tiles - 1 - t : t;
+      const int64_t b = tt / tiles_per_batch;
+      const int64_t r = tt - b * tiles_per_batch;
       const int mb = (int)(r / p.tiles_n);
       const int nb = (int)(r % p.tiles_n);
       const int64_t row0 = (int64_t)mb * (2 * BM) + rank * BM;
@@ -851,6 +858,7 @@ int launch_tc(const GemmDesc& g, int* err, cudaStream_t s) {
   p.rope_cols = ROPE ? g.rope_cols : 0;
   p.ln_stats = g.ln_stats;
   p.ln_colsum = g.ln_colsum;
+  p.reverse = g.reverse;
   const int64_t grid64 =
       p.total_tiles < sm_count() ? p.total_tiles : (int64_t)sm_count();
   gemm_f16_tc<BN, ROPE, LN><<<(int)grid64, kGemmThreads, Cfg::SMEM_BYTES, s>>>(ta, tb,
@@ -914,6 +922,7 @@ int launch_pair(const GemmDesc& g, int* err, cudaStream_t s) {
   p.rope_cols = ROPE ? g.rope_cols : 0;
   p.ln_stats = g.ln_stats;
   p.ln_colsum = g.ln_colsum;
+  p.reverse = g.reverse;
   const int64_t pairs =
       p.total_tiles < g_pair_clusters ? p.total_tiles : (int64_t)g_pair_clusters;
   cudaLaunchConfig_t cfg = {};
@@ -1046,11 +1055,13 @@ int choose_tiling(const GemmDesc& g) {
   return c_pair <= c_256 ? kTilePair : kTile256;
 }
 
-int launch_gemm(const GemmDesc& g, int* err, cudaStream_t s) {
+int launch_gemm(const GemmDesc& desc, int* err, cudaStream_t s) {
+  GemmDesc g = desc;
   if (g.batch < 0 || g.M < 0 || g.K <= 0 || g.N <= 0 || g.act < 0 ||
       g.act > 2 || !g.A || !g.B || !g.out)
     return HEXLIB_B200_ERR_INVAL_PARAMS;
   if (g.batch == 0 || g.M == 0) return HEXLIB_B200_OK;
+  g.reverse = order_next();
   const bool rope = g.rope_cols > 0;
   if (rope && (g.rope_cols % 64 || g.rope_cols > g.N || g.N % 64 || g.rope_T <= 0 ||
                (g.rope_stride != 0 && g.rope_stride != 16 && g.rope_stride != 32) ||

@@ -300,17 +300,19 @@ __global__ void __launch_bounds__(kThreads) layernorm_rows(const uint4* __restri
                                                            const float* __restrict__ w,
                                                            const float* __restrict__ b,
                                                            uint4* __restrict__ y, int64_t R,
-                                                           float eps) {
+                                                           float eps, int rev) {
   constexpr int C = G * V * 8;
   __shared__ float red[kThreads / 32];
   const RowWalk<G> rw;
+  // the k-th row walked is row k, or row R - 1 - k when rev
+  auto at = [&](int64_t k) { return rev ? R - 1 - k : k; };
   uint4 nxt[V];
-  if (rw.first + rw.sub < R) row_load<G, V>(nxt, x, rw.first + rw.sub, rw.g);
+  if (rw.first + rw.sub < R) row_load<G, V>(nxt, x, at(rw.first + rw.sub), rw.g);
   for (int64_t base = rw.first; base < R; base += rw.step) {
     const int64_t r = base + rw.sub;
     float v[V][8];
     unpack_rows<V>(v, nxt);
-    if (r + rw.step < R) row_load<G, V>(nxt, x, r + rw.step, rw.g);
+    if (r + rw.step < R) row_load<G, V>(nxt, x, at(r + rw.step), rw.g);
     float s = 0.f;
 #pragma unroll
     for (int j = 0; j < V; ++j)
@@ -343,7 +345,7 @@ __global__ void __launch_bounds__(kThreads) layernorm_rows(const uint4* __restri
           o.h2[q] = __floats2half2_rn((v[j][2 * q] - mean) * inv * ww[2 * q] + bb[2 * q],
                                       (v[j][2 * q + 1] - mean) * inv * ww[2 * q + 1] +
                                           bb[2 * q + 1]);
-        y[r * (G * V) + j * G + rw.g] = o.u;
+        y[at(r) * (G * V) + j * G + rw.g] = o.u;
       }
     }
   }
@@ -1143,7 +1145,8 @@ int launch_layernorm_f16(const void* x, const float* w, const float* b,
   if (R == 0) return HEXLIB_B200_OK;
   const bool al = aligned16(x) && aligned16(y) && aligned16(w) && aligned16(b);
   const RowCfg cfg = al ? row_cfg(C) : RowCfg{0, 0};
-  HB_ROW_SWITCH(layernorm_rows, cfg, R, s, (const uint4*)x, w, b, (uint4*)y, R, eps)
+  HB_ROW_SWITCH(layernorm_rows, cfg, R, s, (const uint4*)x, w, b, (uint4*)y, R, eps,
+                order_next())
   layernorm_f16_generic<<<grid_for(R * 32, kThreads), kThreads, 0, s>>>(
       (const __half*)x, w, b, (__half*)y, R, C, eps);
   HB_LAUNCH_CHECK();
