@@ -220,6 +220,15 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
 
+// Bring one box of a tensor into L2 ahead of its load (no shared memory, no
+// barrier; x must be 16-byte aligned like any tiled TMA coordinate).
+__device__ __forceinline__ void tma_prefetch_l2_3d(const CUtensorMap* map, int c0, int c1,
+                                                   int c2) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];"
+               ::"l"(map), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+
 __device__ __forceinline__ void tma_load_3d(const CUtensorMap* map,
                                             uint64_t* bar, void* smem_dst,
                                             int c0, int c1, int c2) {
