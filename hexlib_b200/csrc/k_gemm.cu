@@ -225,11 +225,6 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
 #pragma unroll 1
   for (int g = g_lo; g < g_hi; ++g) {
     uint8_t* box = RES_SMEM ? stage + (g - g_lo) * 4096 : stage;
-    if constexpr (!RES_SMEM) {
-      // the previous group's store must have finished reading the stage
-      if (lane == 0) bulk_wait_read_all();
-      __syncwarp();
-    }
     uint32_t packed[2][16];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -323,6 +318,13 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
     }
     if constexpr (ROPE) {
       if (rope_row_ok && n0 + g * 64 < p.rope_cols) rope_head64(packed[0], packed[1], rc, rs);
+    }
+    if constexpr (!RES_SMEM) {
+      // the previous group's store must have finished reading the stage;
+      // waited for only now, so that store overlaps this group's TMEM
+      // loads and arithmetic
+      if (lane == 0) bulk_wait_read_all();
+      __syncwarp();
     }
     // 8 x 16 B into the 128-byte row rl of the stage, swizzled
 #pragma unroll
