@@ -173,7 +173,11 @@ __device__ __forceinline__ void rope_row(const GemmParams& p, int64_t tok, float
 // accumulator is turned into LayerNorm(x) @ W + bias by the row's (mean,
 // rstd) and the weight's column sums: rstd * (acc - mean * colsum) + bias,
 // with bias holding beta @ W + the GEMM's own bias.
-template <bool ROPE, bool RES_SMEM = false, bool LN = false>
+//
+// DBL: two staging boxes per warp (group g - g_lo in box g - g_lo): a box is
+// rewritten once the store issued from it one group earlier -- not the
+// previous group's store -- has read it.
+template <bool ROPE, bool RES_SMEM = false, bool LN = false, bool DBL = false>
 __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtensorMap* tmC,
                                               uint32_t tacc, uint8_t* stage, int quarter,
                                               int lane, int g_lo, int g_hi, int64_t b,
@@ -224,7 +228,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
   if (rrow && g_lo < g_hi) load_res(g_lo, 0, res[0]);
 #pragma unroll 1
   for (int g = g_lo; g < g_hi; ++g) {
-    uint8_t* box = RES_SMEM ? stage + (g - g_lo) * 4096 : stage;
+    uint8_t* box = (RES_SMEM || DBL) ? stage + (g - g_lo) * 4096 : stage;
     uint32_t packed[2][16];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -323,7 +327,10 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
       // the previous group's store must have finished reading the stage;
       // waited for only now, so that store overlaps this group's TMEM
       // loads and arithmetic
-      if (lane == 0) bulk_wait_read_all();
+      if (lane == 0) {
+        if constexpr (DBL) bulk_wait_read_all_but_1();
+        else bulk_wait_read_all();
+      }
       __syncwarp();
     }
     // 8 x 16 B into the 128-byte row rl of the stage, swizzled
@@ -538,12 +545,12 @@ enum { kPairPlain = 0, kPairRope = 1, kPairRes = 2, kPairLn = 3, kPairLnRope = 4
 template <int MODE>
 struct PairCfg {
   static constexpr int BN = 256;                     // columns of the pair's tile
-  static constexpr int STAGES = MODE == kPairRes ? 5 : 6;
+  static constexpr int STAGES = 5;
   static constexpr int A_BYTES = BM * BK * 2;        // 16 KiB: this CTA's 128 rows
   static constexpr int B_BYTES = (BN / 2) * BK * 2;  // 16 KiB: this CTA's 128 columns
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;           // two fp32 accumulators
-  static constexpr int STAGING = kEpiWarps * (MODE == kPairRes ? 8192 : 4096);
+  static constexpr int STAGING = kEpiWarps * 8192;   // two 32x64 fp16 boxes per warp
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGING + 1024 + 256;
 };
 
@@ -740,7 +747,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           goto done;
         }
       }
-      epilogue_tile<ROPE, RES, LN>(p, &tmC, tmem_base + (uint32_t)(acc * BN), stage, quarter,
+      epilogue_tile<ROPE, RES, LN, !RES>(p, &tmC, tmem_base + (uint32_t)(acc * BN), stage, quarter,
                                lane, g_lo, g_hi, b, row0, nb * BN);
       tc_fence_before();
       __syncwarp();
