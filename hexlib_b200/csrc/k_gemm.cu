@@ -532,12 +532,14 @@ done:
 // A wait that gives up raises the abort flag of both CTAs, so the pair
 // unwinds together and meets at the closing cluster barrier.
 //
-// Epilogue modes: kPairPlain (bias, activation, or a residual read from
-// global memory), kPairRope, and kPairRes: each epilogue warp TMA-loads its
-// two 32x64 residual boxes into its staging (8 KiB per warp, one fewer
-// stage) as soon as the previous tile's stores have read it -- before the
-// accumulator is ready -- so the residual's DRAM latency hides under the
-// mainloop instead of stalling the epilogue.
+// Every mode gives each epilogue warp two 32x64 staging boxes (8 KiB per
+// warp, a 5-stage operand ring). Epilogue modes: kPairPlain (bias,
+// activation, or a residual read from global memory) and kPairRope write
+// their two column groups into alternate boxes; kPairRes: each epilogue warp
+// TMA-loads its two residual boxes into the staging as soon as the previous
+// tile's stores have read it -- before the accumulator is ready -- so the
+// residual's DRAM latency hides under the mainloop instead of stalling the
+// epilogue.
 // kPairLn / kPairLnRope: the LayerNorm epilogue (see epilogue_tile), without
 // or with RoPE.
 enum { kPairPlain = 0, kPairRope = 1, kPairRes = 2, kPairLn = 3, kPairLnRope = 4 };
