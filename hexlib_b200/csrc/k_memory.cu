@@ -996,6 +996,7 @@ int memory_kernels_init() {
 #define HB_NOTE_ROWS(K)                                                             \
   note((const void*)K<8, 1>); note((const void*)K<16, 1>); note((const void*)K<32, 1>); \
   note((const void*)K<32, 2>); note((const void*)K<32, 3>); note((const void*)K<32, 4>); \
+  note((const void*)K<16, 6>);                                                              \
   note((const void*)K<256, 1>); note((const void*)K<256, 2>); note((const void*)K<256, 4>);
   HB_NOTE_ROWS(layernorm_rows)
   HB_NOTE_ROWS(ln_stats_rows)
@@ -1134,6 +1135,7 @@ int launch_rows(F* kern, int g, int64_t R, cudaStream_t s, A... args) {
     case 32 * 16 + 2: return launch_rows(K<32, 2>, 32, R, s, __VA_ARGS__);         \
     case 32 * 16 + 3: return launch_rows(K<32, 3>, 32, R, s, __VA_ARGS__);         \
     case 32 * 16 + 4: return launch_rows(K<32, 4>, 32, R, s, __VA_ARGS__);         \
+    case 16 * 16 + 6: return launch_rows(K<16, 6>, 16, R, s, __VA_ARGS__);         \
     case 256 * 16 + 1: return launch_rows(K<256, 1>, 256, R, s, __VA_ARGS__);      \
     case 256 * 16 + 2: return launch_rows(K<256, 2>, 256, R, s, __VA_ARGS__);      \
     case 256 * 16 + 4: return launch_rows(K<256, 4>, 256, R, s, __VA_ARGS__);      \
@@ -1144,7 +1146,10 @@ int launch_layernorm_f16(const void* x, const float* w, const float* b,
   if (R < 0 || C <= 0) return HEXLIB_B200_ERR_INVAL_PARAMS;
   if (R == 0) return HEXLIB_B200_OK;
   const bool al = aligned16(x) && aligned16(y) && aligned16(w) && aligned16(b);
-  const RowCfg cfg = al ? row_cfg(C) : RowCfg{0, 0};
+  RowCfg cfg = al ? row_cfg(C) : RowCfg{0, 0};
+  // C = 768: two rows per warp, 16 lanes x 6 vectors each, so one chain of
+  // shuffles reduces both rows
+  if (cfg.g == 32 && cfg.v == 3) cfg = RowCfg{16, 6};
   HB_ROW_SWITCH(layernorm_rows, cfg, R, s, (const uint4*)x, w, b, (uint4*)y, R, eps,
                 order_next())
   layernorm_f16_generic<<<grid_for(R * 32, kThreads), kThreads, 0, s>>>(
