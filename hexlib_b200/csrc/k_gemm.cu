@@ -1058,7 +1058,8 @@ int gemm_kernels_init() {
 // lighter fill traffic pays where the mainloop bounds the tile (cost 1.0,
 // 1.03 for a single-CTA tile); with a GELU epilogue the epilogue bounds it
 // and the pair's cluster handshakes cost a little (1.05). 128x128 tiles
-// were slower at every measured shape and are used only when pinned:
+// were slower at every measured shape of 8K rows and more, and are chosen
+// only for GEMMs too small to fill the device once (below) or when pinned:
 // HEXLIB_B200_GEMM_TILE = pair, 256 or 128 pins one (for measurements).
 enum { kTileAuto = 0, kTilePair = 1, kTile256 = 2, kTile128 = 3 };
 int g_tile_pin = -1;
@@ -1075,6 +1076,13 @@ int choose_tiling(const GemmDesc& g) {
   if (g_tile_pin == kTile128) return kTile128;
   if (!pair_ok) return kTile256;
   auto rounds = [](int64_t tiles, int64_t slots) { return (tiles + slots - 1) / slots; };
+  // A GEMM whose pair tiles cannot fill the device even once runs on
+  // 128x128 tiles when those fit in one round: twice the CTAs, half the work
+  // each (measured at 256 rows, the 256^2 x 1 encoder: 982 -> 1164
+  // images/s). Larger GEMMs keep the model below.
+  const int64_t t_pair = ((g.M + 255) / 256) * (g.N / 256);
+  const int64_t t_128 = ((g.M + 127) / 128) * ((g.N + 127) / 128);
+  if (t_pair < g_pair_clusters && t_128 <= sm_count()) return kTile128;
   const double c_pair = (double)rounds(((g.M + 255) / 256) * (g.N / 256), g_pair_clusters) *
                         (g.act != 0 ? 1.05 : 1.0);
   const double c_256 = (double)rounds(((g.M + 127) / 128) * (g.N / 256), sm_count()) * 1.03;
