@@ -1060,29 +1060,33 @@ int gemm_kernels_init() {
 // and the pair's cluster handshakes cost a little (1.05). 128x128 tiles
 // were slower at every measured shape of 8K rows and more, and are chosen
 // only for GEMMs too small to fill the device once (below) or when pinned:
-// HEXLIB_B200_GEMM_TILE = pair, 256 or 128 pins one (for measurements).
-enum { kTileAuto = 0, kTilePair = 1, kTile256 = 2, kTile128 = 3 };
+// HEXLIB_B200_GEMM_TILE = pair, 256, 128 or 64 pins one (for measurements).
+enum { kTileAuto = 0, kTilePair = 1, kTile256 = 2, kTile128 = 3, kTile64 = 4 };
 int g_tile_pin = -1;
 
 int choose_tiling(const GemmDesc& g) {
   if (g_tile_pin < 0) {
     const char* e = getenv("HEXLIB_B200_GEMM_TILE");
     g_tile_pin = !e ? kTileAuto
-               : (e[0] == 'p' ? kTilePair : (e[0] == '2' ? kTile256 : (e[0] == '1' ? kTile128 : kTileAuto)));
+               : (e[0] == 'p' ? kTilePair : (e[0] == '2' ? kTile256 : (e[0] == '1' ? kTile128 : (e[0] == '6' ? kTile64 : kTileAuto))));
   }
   const bool pair_ok = g_pair_clusters > 0 && g.b_shared && g.batch == 1;
   if (g_tile_pin == kTilePair && pair_ok) return kTilePair;
   if (g_tile_pin == kTile256) return kTile256;
   if (g_tile_pin == kTile128) return kTile128;
+  if (g_tile_pin == kTile64) return kTile64;
   if (!pair_ok) return kTile256;
   auto rounds = [](int64_t tiles, int64_t slots) { return (tiles + slots - 1) / slots; };
-  // A GEMM whose pair tiles cannot fill the device even once runs on
-  // 128x128 tiles when those fit in one round: twice the CTAs, half the work
-  // each (measured at 256 rows, the 256^2 x 1 encoder: 982 -> 1164
-  // images/s). Larger GEMMs keep the model below: at 4096 rows (256^2 x 16)
-  // 128x128 tiles everywhere measured 19 % slower.
+  // A GEMM whose pair tiles cannot fill the device even once runs on the
+  // narrowest single-CTA tiles that still fit in one round: more CTAs, less
+  // work each (measured at 256 rows, the 256^2 x 1 encoder: 982 images/s on
+  // pair tiles, 1164 on 128x128, 1215 on 128x64). Larger GEMMs keep the
+  // model below: at 4096 rows (256^2 x 16) 128x128 tiles everywhere
+  // measured 19 % slower.
   const int64_t t_pair = ((g.M + 255) / 256) * (g.N / 256);
   const int64_t t_128 = ((g.M + 127) / 128) * ((g.N + 127) / 128);
+  const int64_t t_64 = ((g.M + 127) / 128) * ((g.N + 63) / 64);
+  if (t_pair < g_pair_clusters && t_64 <= sm_count()) return kTile64;
   if (t_pair < g_pair_clusters && t_128 <= sm_count()) return kTile128;
   const double c_pair = (double)rounds(((g.M + 255) / 256) * (g.N / 256), g_pair_clusters) *
                         (g.act != 0 ? 1.05 : 1.0);
@@ -1130,6 +1134,8 @@ int launch_gemm(const GemmDesc& desc, int* err, cudaStream_t s) {
       rc = launch_tc<128, true>(g, err, s);
     else if (tiling == kTile128)
       rc = launch_tc<128, false>(g, err, s);
+    else if (tiling == kTile64)
+      rc = rope ? launch_tc<64, true>(g, err, s) : launch_tc<64, false>(g, err, s);
     else if (g.N % 256 == 0)
       rc = rope ? launch_tc<256, true>(g, err, s) : launch_tc<256, false>(g, err, s);
     else if (g.N % 128 == 0)
