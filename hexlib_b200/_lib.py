@@ -44,6 +44,8 @@ _PROTOS: dict[str, list] = {
                                   c_vp, c_u32, ctypes.POINTER(c_u32)],
     "hexlib_b200_sync": [c_vp],
     "hexlib_b200_diag_wait_timeout": [c_vp, c_u32],
+    "hexlib_b200_diag_wait_timeout_stream": [c_u32, c_vp],
+    "hexlib_b200_stream_status": [c_vp],
     "hexlib_b200_check_batch": [c_vp, c_u32, ctypes.POINTER(c_u64), c_u32,
                                 c_u32, c_vp, c_u32, ctypes.POINTER(c_u32)],
     "hexlib_b200_add_fp16": [c_vp, c_vp, c_vp, c_int, c_vp],

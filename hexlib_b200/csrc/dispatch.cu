@@ -36,11 +36,17 @@ namespace hb {
 namespace {
 thread_local int t_walk = 0;
 bool walk_alternates() {
+#ifdef HEXLIB_B200_MEASUREMENT_KNOBS
+  // Measurement builds only: HEXLIB_B200_WALK_ORDER=ascending keeps every
+  // launch walking its work in ascending order.
   static const bool alt = [] {
     const char* e = getenv("HEXLIB_B200_WALK_ORDER");
     return !(e && strcmp(e, "ascending") == 0);
   }();
   return alt;
+#else
+  return true;
+#endif
 }
 }  // namespace
 

@@ -19,33 +19,67 @@ int attention_kernels_init();
 int diag_kernels_init();
 
 namespace {
-std::once_flag g_init_once;
-int g_init_status = HEXLIB_B200_ERR_INTERNAL;
+constexpr int kMaxDevices = 64;
+std::once_flag g_dev_once[kMaxDevices];
+int g_dev_status[kMaxDevices];
+std::once_flag g_word_once;
+int g_word_status = HEXLIB_B200_ERR_INTERNAL;
+int* g_err_host = nullptr;
 int* g_err_dev = nullptr;
 }  // namespace
 
-int kernels_init() {
-  std::call_once(g_init_once, [] {
+// Function attributes (the dynamic shared memory each kernel may take) belong
+// to the device that is current when they are set, so every device a process
+// uses runs this once, with that device current. It allocates nothing.
+int kernels_init_device() {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    return HEXLIB_B200_ERR_CUDA;
+  }
+  std::call_once(g_dev_once[dev], [dev] {
     int rc = memory_kernels_init();
     if (rc == HEXLIB_B200_OK) rc = gemm_kernels_init();
     if (rc == HEXLIB_B200_OK) rc = quant_kernels_init();
     if (rc == HEXLIB_B200_OK) rc = attention_kernels_init();
     if (rc == HEXLIB_B200_OK) rc = diag_kernels_init();
-    int* host = nullptr;
-    if (rc == HEXLIB_B200_OK &&
-        cudaHostAlloc(reinterpret_cast<void**>(&host), sizeof(int),
-                      cudaHostAllocMapped) == cudaSuccess) {
-      *host = 0;
-      if (cudaHostGetDevicePointer(reinterpret_cast<void**>(&g_err_dev), host,
-                                   0) != cudaSuccess)
-        rc = HEXLIB_B200_ERR_CUDA;
-    } else if (rc == HEXLIB_B200_OK) {
-      rc = HEXLIB_B200_ERR_CUDA;
-    }
     if (rc != HEXLIB_B200_OK) cudaGetLastError();
-    g_init_status = rc;
+    g_dev_status[dev] = rc;
   });
-  return g_init_status;
+  return g_dev_status[dev];
+}
+
+// The per-kernel entries' error word: one int of mapped, portable host memory
+// that every device can write (a bounded wait that expires sets it to 1) and
+// the host reads after the stream has drained (hexlib_b200_stream_status).
+int kernels_init() {
+  const int rc = kernels_init_device();
+  if (rc != HEXLIB_B200_OK) return rc;
+  std::call_once(g_word_once, [] {
+    int st = HEXLIB_B200_ERR_CUDA;
+    int* host = nullptr;
+    if (cudaHostAlloc(reinterpret_cast<void**>(&host), sizeof(int),
+                      cudaHostAllocMapped | cudaHostAllocPortable) == cudaSuccess) {
+      *host = 0;
+      if (cudaHostGetDevicePointer(reinterpret_cast<void**>(&g_err_dev), host, 0) ==
+          cudaSuccess) {
+        g_err_host = host;
+        st = HEXLIB_B200_OK;
+      }
+    }
+    if (st != HEXLIB_B200_OK) cudaGetLastError();
+    g_word_status = st;
+  });
+  return g_word_status;
+}
+
+// Reads and clears the per-kernel entries' error word; true if it was set.
+bool take_default_error() {
+  if (!g_err_host) return false;
+  volatile int* e = g_err_host;
+  const bool set = *e != 0;
+  *e = 0;
+  return set;
 }
 
 int* default_error_word() { return g_err_dev; }
@@ -377,6 +411,23 @@ int hexlib_b200_attention_fp16(const void* q, const void* k, const void* v,
     return HEXLIB_B200_ERR_INVAL_PARAMS;
   return hb::launch_attention(q, k, v, ctx, Bn, T, D, scale,
                               hb::default_error_word(), as_stream(stream));
+}
+
+int hexlib_b200_stream_status(void* stream) {
+  if (cudaStreamSynchronize(as_stream(stream)) != cudaSuccess) {
+    cudaGetLastError();
+    return HEXLIB_B200_ERR_CUDA;
+  }
+  bool noalloc_set = false;
+  const int rc = hb::noalloc_take_error(&noalloc_set);
+  const bool default_set = hb::take_default_error();
+  if (rc != HEXLIB_B200_OK) return rc;
+  return (default_set || noalloc_set) ? HEXLIB_B200_ERR_TIMEOUT : HEXLIB_B200_OK;
+}
+
+int hexlib_b200_diag_wait_timeout_stream(uint32_t limit_us, void* stream) {
+  HB_ENTRY_INIT();
+  return hb::launch_wait_timeout_probe(hb::default_error_word(), limit_us, as_stream(stream));
 }
 
 }  // extern "C"

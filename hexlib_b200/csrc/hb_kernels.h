@@ -143,12 +143,25 @@ int launch_attention_qkv(const void* qkv, void* ctx, int64_t B, int T, int H, in
 // timeout in `err` after `limit_us` and returns.
 int launch_wait_timeout_probe(int* err, uint32_t limit_us, cudaStream_t s);
 
-// One-time per-process setup of kernel attributes (dynamic shared memory
-// limits); safe to call repeatedly. Returns a status.
+// Setup of kernel attributes (dynamic shared memory limits) on the current
+// device, once per device; allocates nothing. Returns a status.
+int kernels_init_device();
+
+// kernels_init_device() plus the one-time allocation of the error word of
+// the per-kernel entry points; safe to call repeatedly. Returns a status.
 int kernels_init();
 
 // The session-independent device error word that kernels launched through
 // the public per-kernel entry points report bounded-wait timeouts in.
 int* default_error_word();
+
+// Reads and clears that word (after the caller has drained its stream);
+// true if a bounded wait had expired.
+bool take_default_error();
+
+// Reads and clears the current device's error word of the non-allocating
+// q4_0 entry point (a no-op before that entry has run on the device); sets
+// *set when a bounded wait had expired. Returns a status.
+int noalloc_take_error(bool* set);
 
 }  // namespace hb

@@ -32,6 +32,7 @@
 #include <stdint.h>
 #include <stdlib.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "hb_device.cuh"
@@ -902,8 +903,11 @@ bool aligned16(const void* p) {
 
 // Pairs that fit on the device at once (0: the pair kernel is not used),
 // found once by the occupancy calculator for clusters of two.
-int g_pair_clusters = 0;
-bool g_pair_res = false;
+// Resident CTA-pair clusters per device (0: the pair kernel is unavailable)
+// and whether the residual is TMA-staged; published once by
+// gemm_kernels_init, read by every launch on any host thread.
+std::atomic<int> g_pair_clusters{0};
+std::atomic<bool> g_pair_res{false};
 
 template <bool ROPE, bool LN = false>
 int launch_pair(const GemmDesc& g, int* err, cudaStream_t s) {
@@ -920,7 +924,7 @@ int launch_pair(const GemmDesc& g, int* err, cudaStream_t s) {
   if (!make_tmap_3d_f16(&tcm, g.out, (uint64_t)g.N, (uint64_t)g.M, (uint64_t)g.batch, 64, 32))
     return -1;
   // the residual, read through TMA boxes shaped like the output's
-  const bool res_tma = !ROPE && !LN && g.resid && g_pair_res &&
+  const bool res_tma = !ROPE && !LN && g.resid && g_pair_res.load(std::memory_order_relaxed) &&
                        make_tmap_3d_f16(&trm, g.resid, (uint64_t)g.N, (uint64_t)g.M,
                                         (uint64_t)g.batch, 64, 32);
   if (!res_tma) trm = tcm;
@@ -949,8 +953,9 @@ int launch_pair(const GemmDesc& g, int* err, cudaStream_t s) {
   p.ln_stats = g.ln_stats;
   p.ln_colsum = g.ln_colsum;
   p.reverse = g.reverse;
-  const int64_t pairs =
-      p.total_tiles < g_pair_clusters ? p.total_tiles : (int64_t)g_pair_clusters;
+  const int64_t clusters = g_pair_clusters.load(std::memory_order_relaxed);
+  if (clusters <= 0) return -1;
+  const int64_t pairs = p.total_tiles < clusters ? p.total_tiles : clusters;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
   cfg.blockDim = dim3(kGemmThreads, 1, 1);
@@ -1003,10 +1008,20 @@ int gemm_kernels_init() {
   cudaFuncAttributes fa;
   cudaError_t e7 = cudaFuncGetAttributes(&fa, gemm_f16_simt);
   sm_count();
-  // The pair kernel: HEXLIB_B200_GEMM_PAIR=0 turns it off (for comparisons).
-  g_pair_clusters = 0;
-  const char* env = getenv("HEXLIB_B200_GEMM_PAIR");
-  if (!(env && env[0] == '0') &&
+  bool pair_on = true, pair_res_on = true;
+#ifdef HEXLIB_B200_MEASUREMENT_KNOBS
+  // Measurement builds only: HEXLIB_B200_GEMM_PAIR=0 turns the pair kernel
+  // off and HEXLIB_B200_GEMM_PAIR_RES=0 its TMA-staged residual.
+  {
+    const char* env = getenv("HEXLIB_B200_GEMM_PAIR");
+    const char* er = getenv("HEXLIB_B200_GEMM_PAIR_RES");
+    pair_on = !(env && env[0] == '0');
+    pair_res_on = !(er && er[0] == '0');
+  }
+#endif
+  int clusters = 0;
+  bool res = false;
+  if (pair_on &&
       cudaFuncSetAttribute(gemm_f16_pair<kPairPlain>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                            PairCfg<kPairPlain>::SMEM_BYTES) == cudaSuccess &&
@@ -1017,12 +1032,10 @@ int gemm_kernels_init() {
     cudaFuncSetAttribute(gemm_f16_pair<kPairLnRope>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                          PairCfg<kPairLnRope>::SMEM_BYTES);
-    // the TMA-staged residual: HEXLIB_B200_GEMM_PAIR_RES=0 turns it off
-    const char* er = getenv("HEXLIB_B200_GEMM_PAIR_RES");
-    g_pair_res = !(er && er[0] == '0') &&
-                 cudaFuncSetAttribute(gemm_f16_pair<kPairRes>,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      PairCfg<kPairRes>::SMEM_BYTES) == cudaSuccess;
+    res = pair_res_on &&
+          cudaFuncSetAttribute(gemm_f16_pair<kPairRes>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               PairCfg<kPairRes>::SMEM_BYTES) == cudaSuccess;
     cudaGetLastError();
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (unsigned)sm_count(), 1, 1);
@@ -1038,9 +1051,14 @@ int gemm_kernels_init() {
     int n = 0;
     if (cudaOccupancyMaxActiveClusters(&n, gemm_f16_pair<kPairPlain>, &cfg) == cudaSuccess &&
         n > 0)
-      g_pair_clusters = n;
+      clusters = n;
     cudaGetLastError();
   }
+  // Every device of a process is a B200 with the same answer; the values are
+  // stored, never cleared, so a launch on another thread reads either the
+  // initial "no pair kernel" or the final figures.
+  g_pair_res.store(res, std::memory_order_relaxed);
+  g_pair_clusters.store(clusters, std::memory_order_relaxed);
   if (e1 != cudaSuccess || e2 != cudaSuccess || e3 != cudaSuccess || e4 != cudaSuccess ||
       e5 != cudaSuccess || e6 != cudaSuccess || e7 != cudaSuccess || e8 != cudaSuccess ||
       e9 != cudaSuccess) {
@@ -1059,22 +1077,35 @@ int gemm_kernels_init() {
 // 1.03 for a single-CTA tile); with a GELU epilogue the epilogue bounds it
 // and the pair's cluster handshakes cost a little (1.05). 128x128 tiles
 // were slower at every measured shape of 8K rows and more, and are chosen
-// only for GEMMs too small to fill the device once (below) or when pinned:
-// HEXLIB_B200_GEMM_TILE = pair, 256, 128 or 64 pins one (for measurements).
+// only for GEMMs too small to fill the device once (below). A measurement
+// build (HEXLIB_B200_MEASUREMENT_KNOBS) can pin one with HEXLIB_B200_GEMM_TILE
+// = pair, 256, 128 or 64; the library as shipped reads no environment.
 enum { kTileAuto = 0, kTilePair = 1, kTile256 = 2, kTile128 = 3, kTile64 = 4 };
-int g_tile_pin = -1;
+
+int tile_pin() {
+#ifdef HEXLIB_B200_MEASUREMENT_KNOBS
+  static const int pin = [] {
+    const char* e = getenv("HEXLIB_B200_GEMM_TILE");
+    return !e ? kTileAuto
+              : (e[0] == 'p' ? kTilePair
+                             : (e[0] == '2' ? kTile256
+                                            : (e[0] == '1' ? kTile128
+                                                           : (e[0] == '6' ? kTile64 : kTileAuto))));
+  }();
+  return pin;
+#else
+  return kTileAuto;
+#endif
+}
 
 int choose_tiling(const GemmDesc& g) {
-  if (g_tile_pin < 0) {
-    const char* e = getenv("HEXLIB_B200_GEMM_TILE");
-    g_tile_pin = !e ? kTileAuto
-               : (e[0] == 'p' ? kTilePair : (e[0] == '2' ? kTile256 : (e[0] == '1' ? kTile128 : (e[0] == '6' ? kTile64 : kTileAuto))));
-  }
-  const bool pair_ok = g_pair_clusters > 0 && g.b_shared && g.batch == 1;
-  if (g_tile_pin == kTilePair && pair_ok) return kTilePair;
-  if (g_tile_pin == kTile256) return kTile256;
-  if (g_tile_pin == kTile128) return kTile128;
-  if (g_tile_pin == kTile64) return kTile64;
+  const int pin = tile_pin();
+  const int pair_clusters = g_pair_clusters.load(std::memory_order_relaxed);
+  const bool pair_ok = pair_clusters > 0 && g.b_shared && g.batch == 1;
+  if (pin == kTilePair && pair_ok) return kTilePair;
+  if (pin == kTile256) return kTile256;
+  if (pin == kTile128) return kTile128;
+  if (pin == kTile64) return kTile64;
   if (!pair_ok) return kTile256;
   auto rounds = [](int64_t tiles, int64_t slots) { return (tiles + slots - 1) / slots; };
   // A GEMM whose pair tiles cannot fill the device even once runs on the
@@ -1086,9 +1117,9 @@ int choose_tiling(const GemmDesc& g) {
   const int64_t t_pair = ((g.M + 255) / 256) * (g.N / 256);
   const int64_t t_128 = ((g.M + 127) / 128) * ((g.N + 127) / 128);
   const int64_t t_64 = ((g.M + 127) / 128) * ((g.N + 63) / 64);
-  if (t_pair < g_pair_clusters && t_64 <= sm_count()) return kTile64;
-  if (t_pair < g_pair_clusters && t_128 <= sm_count()) return kTile128;
-  const double c_pair = (double)rounds(((g.M + 255) / 256) * (g.N / 256), g_pair_clusters) *
+  if (t_pair < pair_clusters && t_64 <= sm_count()) return kTile64;
+  if (t_pair < pair_clusters && t_128 <= sm_count()) return kTile128;
+  const double c_pair = (double)rounds(((g.M + 255) / 256) * (g.N / 256), pair_clusters) *
                         (g.act != 0 ? 1.05 : 1.0);
   const double c_256 = (double)rounds(((g.M + 127) / 128) * (g.N / 256), sm_count()) * 1.03;
   return c_pair <= c_256 ? kTilePair : kTile256;

@@ -12,9 +12,12 @@
 // host error word is not used.
 //
 // What must start at zero: only the error word, which the module load zeroes
-// and which a device-side bounded wait sets to 1 if it ever expires. The
-// weight scratch needs no initial value: each call's dequantization writes
-// every byte its GEMM then reads.
+// and which a device-side bounded wait sets to 1 if it ever expires; the
+// caller learns of it, and the word is cleared, through
+// hexlib_b200_stream_status after the stream has drained (the call itself
+// returns as soon as the work is queued, so it cannot report it). The weight
+// scratch needs no initial value: each call's dequantization writes every
+// byte its GEMM then reads.
 //
 // Calls share the one scratch per device: two calls that overlap in time (on
 // different streams, or from different host threads without ordering) race
@@ -31,9 +34,6 @@
 
 namespace hb {
 
-int gemm_kernels_init();
-int quant_kernels_init();
-
 namespace {
 
 constexpr uint64_t kScratchBytes = 8ull << 20;
@@ -47,18 +47,12 @@ struct Slots {
   int* err = nullptr;
 };
 
-std::once_flag g_once;
-int g_setup_rc = HEXLIB_B200_ERR_INTERNAL;
 std::mutex g_mu;
 Slots g_slots[kMaxDevices];
 
 int slots_for_current_device(Slots* out) {
-  std::call_once(g_once, [] {
-    int rc = gemm_kernels_init();
-    if (rc == HEXLIB_B200_OK) rc = quant_kernels_init();
-    g_setup_rc = rc;
-  });
-  if (g_setup_rc != HEXLIB_B200_OK) return g_setup_rc;
+  const int init = kernels_init_device();
+  if (init != HEXLIB_B200_OK) return init;
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
     cudaGetLastError();
@@ -82,6 +76,34 @@ int slots_for_current_device(Slots* out) {
 }
 
 }  // namespace
+
+int noalloc_take_error(bool* set) {
+  *set = false;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    return HEXLIB_B200_ERR_CUDA;
+  }
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_slots[dev].err) return HEXLIB_B200_OK;
+  }
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_noalloc_err, sizeof(int)) != cudaSuccess) {
+    cudaGetLastError();
+    return HEXLIB_B200_ERR_CUDA;
+  }
+  if (v != 0) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(g_noalloc_err, &zero, sizeof(int)) != cudaSuccess) {
+      cudaGetLastError();
+      return HEXLIB_B200_ERR_CUDA;
+    }
+    *set = true;
+  }
+  return HEXLIB_B200_OK;
+}
+
 }  // namespace hb
 
 extern "C" int hexlib_b200_matmul_epilogue_q4_0_noalloc(const void* a, const void* w,

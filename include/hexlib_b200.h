@@ -197,6 +197,22 @@ HEXLIB_B200_API int hexlib_b200_check_batch(const uint8_t *batch, uint32_t len,
 HEXLIB_B200_API int hexlib_b200_diag_wait_timeout(hexlib_b200_ctx *ctx,
                                                   uint32_t limit_us);
 
+/* The per-kernel entry points below return as soon as their work is queued,
+ * so a device-side failure cannot be their return value. This waits for
+ * `stream` and reports, then clears, what the kernels launched through them
+ * recorded since the previous call: HEXLIB_B200_ERR_TIMEOUT if a bounded
+ * wait inside one expired (its output is not valid), ERR_CUDA if the stream
+ * reported an error, OK otherwise. The record is per process (per device for
+ * hexlib_b200_matmul_epilogue_q4_0_noalloc), not per stream. No counterpart
+ * in the reference, whose kernel calls are synchronous (skel_dispatch.c:
+ * 248-262). */
+HEXLIB_B200_API int hexlib_b200_stream_status(void *stream);
+
+/* Failure-path diagnostic for the per-kernel entries: queue on `stream` the
+ * kernel of hexlib_b200_diag_wait_timeout, recording into the per-kernel
+ * entries' error word; hexlib_b200_stream_status then answers ERR_TIMEOUT. */
+HEXLIB_B200_API int hexlib_b200_diag_wait_timeout_stream(uint32_t limit_us, void *stream);
+
 /* The status as text (hexlib_dsp.h:71-91). */
 HEXLIB_B200_API const char *hexlib_b200_status_name(int status);
 
@@ -278,7 +294,8 @@ HEXLIB_B200_API int hexlib_b200_matmul_epilogue_q8_0(const void *a, const void *
  * reference, whose kernels always receive a scratch from their caller. Calls
  * that overlap in time share that scratch and race; issue them in order (one
  * stream). The first call on a device looks the array up with that device
- * current; make it before any stream capture begins. */
+ * current; make it before any stream capture begins. A bounded wait that
+ * expires inside it is reported by hexlib_b200_stream_status. */
 HEXLIB_B200_API int hexlib_b200_matmul_epilogue_q4_0_noalloc(const void *a, const void *w,
                                                              const float *bias, void *out,
                                                              int M, int K, int N, int act,

@@ -10,7 +10,8 @@ is a build artefact: it is git-ignored but travels with the tree, so the
 GPU-side tests and the CPU-baseline timing can call the reference's own
 arithmetic where the reference itself is absent.
 
-Usage: python oracle/build_ref.py [/path/to/hexlib-checkout]
+Usage: python oracle/build_ref.py /path/to/hexlib-checkout
+       (or HEXLIB_REFERENCE=/path/to/hexlib-checkout python oracle/build_ref.py)
 """
 from __future__ import annotations
 
@@ -40,9 +41,12 @@ KERNELS = {
 }
 
 
-def build(ref_root: str = "/root/reference") -> str | None:
-    """Build libhexref.so if the reference checkout is present; return its
-    path (an existing prebuilt one is returned when the checkout is absent)."""
+def build(ref_root: str | None) -> str | None:
+    """Build libhexref.so from the reference checkout at `ref_root`; return its
+    path (an existing prebuilt one is returned when no checkout is given or
+    it is absent, as on a GPU box that only runs the prebuilt file)."""
+    if not ref_root:
+        return LIB if os.path.exists(LIB) else None
     kdir = os.path.join(ref_root, "kernels")
     if not os.path.isdir(kdir):
         return LIB if os.path.exists(LIB) else None
@@ -68,4 +72,8 @@ def build(ref_root: str = "/root/reference") -> str | None:
 
 
 if __name__ == "__main__":
-    print(build(sys.argv[1] if len(sys.argv) > 1 else "/root/reference"))
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("HEXLIB_REFERENCE")
+    if not root:
+        sys.exit("usage: python oracle/build_ref.py /path/to/hexlib-checkout "
+                 "(or set HEXLIB_REFERENCE)")
+    print(build(root))

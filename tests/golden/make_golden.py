@@ -272,7 +272,10 @@ def make_quant(ref_root: str) -> None:
 
 if __name__ == "__main__":
     args = [a for a in sys.argv[1:] if not a.startswith("--")]
-    root = args[0] if args else "/root/reference"
+    root = args[0] if args else os.environ.get("HEXLIB_REFERENCE")
+    if not root:
+        sys.exit("usage: python tests/golden/make_golden.py /path/to/hexlib-checkout "
+                 "[--quant-only] (or set HEXLIB_REFERENCE)")
     if "--quant-only" not in sys.argv:
         main(root)
     make_quant(root)

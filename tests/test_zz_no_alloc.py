@@ -36,6 +36,8 @@ def test_two_calls_in_a_row_match_the_workspace_entry(M, K, N, act):
         U.call("hexlib_b200_matmul_epilogue_q4_0_noalloc", U.ptr(da), U.ptr(dw), U.ptr(db),
                U.ptr(y1), M, K, N, act, U.stream())
         np.testing.assert_array_equal(U.host(y1), U.host(y0))
+        # no bounded wait expired in either call
+        assert U.call_rc("hexlib_b200_stream_status", U.stream()) == U.OK
 
 
 def test_a_weight_beyond_the_fixed_scratch_is_refused():
