@@ -84,26 +84,47 @@ def peaks() -> dict:
 
 # ---- CPU baseline ----------------------------------------------------------------
 
-def cpu_port_time(cfg, n_images: int, warm: bool = True) -> tuple[float, int, str]:
-    """Seconds per image of the oracle port (hexlib's reference executor,
-    restated) over `n_images` images, on all BLAS threads of this host."""
-    import numpy as np  # noqa: F401
+def oracle_model(cfg):
+    """The unfused fp16-weight plan and the weight feeds the oracle replays
+    for `cfg`: for q4_0 / q8_0 weights, the same draw quantized as the plan
+    stages it and dequantized to fp16 (the arithmetic the quantized GEMM
+    performs), so the oracle sees exactly the weights the GPU multiplies."""
+    import dataclasses
 
     from hexlib_b200 import feeds as F
     from hexlib_b200 import graph as G
-    from oracle import executor
     g = G.build_vision_encoder(cfg)
-    ep = G.compile_for_cuda(g)
     w = F.weights(cfg, 0, g)
+    if cfg.weight_dtype in ("q4_0", "q8_0"):
+        from hexlib_b200 import quant
+        from oracle import quant as oq
+        for name, t in g.tensors.items():
+            if t.const and t.dtype == cfg.weight_dtype:
+                w[name] = oq.dequantize_f16(quant.quantize(w[name], t.dtype), t.shape, t.dtype)
+        g = G.build_vision_encoder(dataclasses.replace(cfg, weight_dtype="fp16"))
+    return G.compile_for_cuda(g), w
+
+
+def cpu_port_time(cfg, n_images: int, warm: bool = True):
+    """Seconds per image of the oracle port (hexlib's reference executor,
+    restated) over `n_images` images, on all BLAS threads of this host; also
+    the embeddings of the first image (for the parity check)."""
+    from hexlib_b200 import feeds as F
+    from hexlib_b200 import graph as G
+    from oracle import executor
+    ep, w = oracle_model(cfg)
     imgs = F.images(cfg, n_images, 1)
     if warm:  # page in numpy/BLAS on a small model
         small = G.qwen35_at(64)
         gs = G.build_vision_encoder(small)
         executor.run(G.compile_for_cuda(gs), dict(F.weights(small, 0, gs),
                                                   image=F.images(small, 1, 1)[0]))
+    first = None
     t0 = time.perf_counter()
     for i in range(n_images):
-        executor.run(ep, dict(w, image=imgs[i]))
+        out = executor.run(ep, dict(w, image=imgs[i]))
+        if i == 0:
+            first = out[ep.graph.outputs[0]]
     dt = (time.perf_counter() - t0) / n_images
     threads = os.cpu_count() or 1
     try:
@@ -112,7 +133,7 @@ def cpu_port_time(cfg, n_images: int, warm: bool = True) -> tuple[float, int, st
         threads = max([i.get("num_threads", 1) for i in info] + [1])
     except Exception:  # noqa: BLE001
         pass
-    return dt, threads, f"{n_images} image(s) at {cfg.image_size}x{cfg.image_size}"
+    return dt, threads, f"{n_images} image(s) at {cfg.image_size}x{cfg.image_size}", first
 
 
 def run_reference(args) -> None:
@@ -124,7 +145,7 @@ def run_reference(args) -> None:
     # Each image is ~20-30 s of CPU at 512^2: time at most 3 so the arm ends
     # within a few minutes whatever --steps asks for.
     n = max(1, min(args.steps, 3))
-    dt, threads, sample = cpu_port_time(cfg, n, warm=args.warmup > 0)
+    dt, threads, sample, _ = cpu_port_time(cfg, n, warm=args.warmup > 0)
     v = 1.0 / dt
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT,
@@ -219,9 +240,12 @@ class ClockSampler:
 
 # ---- the B200 arm ------------------------------------------------------------------------
 
-def op_work(plan, op_index: int, n_images: int) -> tuple[str, float, str]:
-    """(bound, algorithmic work per launch, unit) for one op of the plan."""
-    import numpy as np  # noqa: F401
+def op_work(plan, op_index: int, n_images: int) -> tuple[str, float, float]:
+    """(bound, FLOPs, bytes) of one op of the plan over `n_images`: FLOPs of
+    its contractions (2·M·N·K per GEMM, 4·T²·D per attention head) and its
+    algorithmic bytes (every input read once, every output written once at
+    its storage dtype). `bound` is "tensor" for the contractions, "hbm" for
+    the rest."""
     from hexlib_b200 import wire
     blob = plan.blob
     hdr = wire.HDR.unpack_from(blob)
@@ -236,27 +260,43 @@ def op_work(plan, op_index: int, n_images: int) -> tuple[str, float, str]:
         p = P[names[n]]
         return p.nbytes * (n_images if p.buffer == 1 else 1)
 
-    if vname in ("matmul_epilogue", "matmul_epilogue_residual", "matmul_epilogue_ln",
-                 "matmul_epilogue_ln_rope"):
+    nbytes = float(sum(nb(s) for s in srcs) + sum(nb(d) for d in dsts))
+    if vname.startswith("matmul_epilogue"):
         a, w = P[names[srcs[0]]], P[names[srcs[1]]]
-        M = a.shape[0] * n_images
         K, N = w.shape
-        return "tensor", 2.0 * M * N * K, "FLOP"
+        return "tensor", 2.0 * a.shape[0] * n_images * N * K, nbytes
     if vname == "matmul":
         a, b = P[names[srcs[0]]], P[names[srcs[1]]]
         Bn, M, K = a.shape
-        return "tensor", 2.0 * Bn * n_images * M * b.shape[2] * K, "FLOP"
+        return "tensor", 2.0 * Bn * n_images * M * b.shape[2] * K, nbytes
     if vname == "attention":
-        q = P[names[srcs[0]]]
-        Bn, T, D = q.shape
-        return "tensor", 4.0 * Bn * n_images * T * T * D, "FLOP"
+        Bn, T, D = P[names[srcs[0]]].shape
+        return "tensor", 4.0 * Bn * n_images * T * T * D, nbytes
     if vname == "attention_qkv":
         T, _, H, D = P[names[srcs[0]]].shape
-        return "tensor", 4.0 * H * n_images * T * T * D, "FLOP"
-    if vname == "matmul_epilogue_rope":
-        a, w = P[names[srcs[0]]], P[names[srcs[1]]]
-        return "tensor", 2.0 * a.shape[0] * n_images * w.shape[0] * w.shape[1], "FLOP"
-    return "hbm", float(sum(nb(s) for s in srcs) + sum(nb(d) for d in dsts)), "B"
+        return "tensor", 4.0 * H * n_images * T * T * D, nbytes
+    return "hbm", 0.0, nbytes
+
+
+def traffic_on_record(kernel: str, image_size: int, n_images: int):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary
+    (profiles/traffic.json), scaled to `n_images` -- only when that capture was
+    taken at this image size (its bytes grow with the images, not with the
+    resolution); else (None, why)."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            tr = json.load(f)
+    except Exception:  # noqa: BLE001
+        return None, "no ncu traffic summary on record"
+    ent = tr.get(kernel)
+    if ent is None:
+        return None, f"no ncu capture of {kernel} on record"
+    if int(ent["image_size"]) != image_size:
+        return None, (f"the ncu capture of {kernel} on record is at {ent['image_size']}^2, "
+                      f"not {image_size}^2")
+    per_image = float(ent["bytes"]) / float(ent["images"])
+    return per_image * n_images, (f"{ent['source']}; {ent['images']} images per captured "
+                                  f"launch, scaled to {n_images}")
 
 
 def run_b200(args) -> None:
@@ -283,10 +323,12 @@ def run_b200(args) -> None:
     g = G.build_vision_encoder(cfg)
     use_att = (not args.no_attention_fusion) and attention_available()
     use_qkv = use_att and not args.no_qkv_fusion
-    ep = G.compile_for_cuda(g, attention=use_att, residual=not args.no_residual_fusion,
-                            qkv=use_qkv, rope_epilogue=args.rope == "epilogue",
-                            ln_fold=args.ln_fold == "on" and args.weights == "fp16",
-                            patch_cast=not args.no_patch_cast)
+    rewrites = dict(G.DEFAULT_REWRITES)
+    rewrites.update(attention=use_att, residual=not args.no_residual_fusion, qkv=use_qkv,
+                    rope_epilogue=args.rope == "epilogue",
+                    ln_fold=args.ln_fold == "on" and args.weights == "fp16",
+                    patch_cast=not args.no_patch_cast)
+    ep = G.compile_for_cuda(g, **rewrites)
     w = F.weights(cfg, 0, g)
     plan = wholeplan.build_cuda_plan(ep, w, alias=True)
     sh = D.shard(args.batch, rank, world)
@@ -302,11 +344,20 @@ def run_b200(args) -> None:
     stream = torch.cuda.ExternalStream(s.stream(), device=torch.device("cuda", local))
     emb = s.device_view(plan.outputs[0], n)
 
-    def step_device():
+    gather_events: list = []
+
+    def step_device(timed=False):
         s.invoke(n, sync=False)
         if pg is not None:
             with torch.cuda.stream(stream):
+                if timed:   # the all-gather's own device time, on the session stream
+                    g0 = torch.cuda.Event(enable_timing=True)
+                    g1 = torch.cuda.Event(enable_timing=True)
+                    g0.record(stream)
                 D.gather_embeddings(emb)
+                if timed:
+                    g1.record(stream)
+                    gather_events.append((g0, g1))
 
     def barrier():
         if pg is not None:
@@ -328,7 +379,7 @@ def run_b200(args) -> None:
     clocks.begin()
     e0.record(stream)
     for _ in range(args.steps):
-        step_device()
+        step_device(timed=True)
     e1.record(stream)
     s.sync()
     e1.synchronize()
@@ -339,6 +390,12 @@ def run_b200(args) -> None:
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
     ms_max = float(t.item())
     value = args.batch * args.steps / (ms_max / 1e3)
+    gather_ms = None
+    if gather_events:
+        t = torch.tensor([sum(a.elapsed_time(b) for a, b in gather_events) / len(gather_events)],
+                         device="cuda")
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        gather_ms = float(t.item())
 
     # ---- end to end through the public Pipeline API (pinned host buffers) ----------
     # Two sessions used in turn: each step uploads its images, replays the
@@ -387,50 +444,57 @@ def run_b200(args) -> None:
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
     e2e = args.batch * args.steps / (float(t.item()) / 1e3)
 
-    # ---- roofline of the dominant kernel (eager, op-by-op timed passes) -------------
-    # Three passes, each op's median: one pass can land on a clock dip.
+    # ---- per-kernel roofline (eager, op-by-op timed passes) -------------------------
+    # Three passes, each op's median: one pass can land on a clock dip. Each op
+    # is timed alone by CUDA events around its launch, so the burst peaks of
+    # MEASURED_PEAKS.json are the denominators.
     passes = [[r.cycles for r in s.invoke(n, mode=MODE_EAGER).results] for _ in range(3)]
     per_op = [sorted(v)[1] for v in zip(*passes)]
+    pk = peaks()
     groups: dict[tuple, list[int]] = {}
+    roof_s = 0.0          # the encoder's roofline time: sum of max(FLOPs/peak, bytes/BW)
     for i, ns in enumerate(per_op):
-        bound, work, unit = op_work(plan, i, n)
-        groups.setdefault((plan.kinds[i], bound, work, unit), []).append(ns)
+        bound, flops, nbytes = op_work(plan, i, n)
+        roof_s += max(flops / (pk["tc"] * 1e12), nbytes / (pk["hbm"] * 1e9))
+        groups.setdefault((plan.kinds[i], bound, flops, nbytes), []).append(ns)
     total_ns = sum(per_op)
     table = sorted(((sum(v), k, v) for k, v in groups.items()), reverse=True)
-    pk = peaks()
-    dom_ns, (dname, dbound, dwork, dunit), dlist = table[0]
+
+    def rate(bound, flops, nbytes, secs):
+        return flops / secs / 1e12 if bound == "tensor" else nbytes / secs / 1e9
+
+    dom_ns, (dname, dbound, dflops, dbytes), dlist = table[0]
     mean_s = (dom_ns / len(dlist)) / 1e9
-    if dbound == "tensor":
-        achieved = dwork / mean_s / 1e12
-        peak, punit = pk["tc_sustained"], "TFLOP/s"
-    else:
-        achieved = dwork / mean_s / 1e9
-        peak, punit = pk["hbm"], "GB/s"
-    traffic, traffic_note = None, "no ncu capture of this kernel on record"
-    try:
-        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
-            tr = json.load(f)
-        ent = tr.get(dname)
-        if ent is not None:
-            traffic = float(ent["bytes_per_launch"])
-            traffic_note = ent.get("source", "")
-    except Exception:  # noqa: BLE001
-        pass
+    achieved = rate(dbound, dflops, dbytes, mean_s)
+    peak, punit = (pk["tc"], "TFLOP/s") if dbound == "tensor" else (pk["hbm"], "GB/s")
+    traffic, traffic_note = traffic_on_record(dname, cfg.image_size, n)
 
     kernels = []
-    for tot, (kname, bound, work, unit), lst in table:
+    for tot, (kname, bound, flops, nbytes), lst in table:
         m = tot / len(lst) / 1e9
+        a = rate(bound, flops, nbytes, m)
         kernels.append({"kernel": kname, "launches": len(lst), "share": tot / total_ns,
-                        "mean_us": m * 1e6,
-                        "achieved": (work / m / 1e12) if bound == "tensor" else (work / m / 1e9),
-                        "unit": "TFLOP/s" if bound == "tensor" else "GB/s"})
+                        "mean_us": m * 1e6, "achieved": a,
+                        "unit": "TFLOP/s" if bound == "tensor" else "GB/s",
+                        "frac": a / (pk["tc"] if bound == "tensor" else pk["hbm"])})
 
-    cpu = None
-    if world == 1 and rank == 0 and os.environ.get("HEXLIB_B200_BENCH_NO_CPU") != "1":
-        dt, threads, sample = cpu_port_time(cfg, 1)
-        cpu = {"value": 1.0 / dt, "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": sample + " through the numpy restatement of hexlib's reference "
-                                  "plan executor (oracle/executor.py)"}
+    # ---- parity: this step's first image against the oracle (untimed) ----------------
+    s.invoke(n)                                  # one more graph replay
+    got0 = s.read_output(plan.outputs[0], 1)[0]
+    cpu, parity = None, None
+    if rank == 0:
+        if world == 1 and os.environ.get("HEXLIB_B200_BENCH_NO_CPU") != "1":
+            dt, threads, sample, ref0 = cpu_port_time(cfg, 1)
+            cpu = {"value": 1.0 / dt, "unit": UNIT, "cores": threads, "kind": "port",
+                   "sample": sample + " through the numpy restatement of hexlib's reference "
+                                      "plan executor (oracle/executor.py)"}
+        else:
+            _, _, _, ref0 = cpu_port_time(cfg, 1, warm=False)
+        err = float(np.abs(got0.astype(np.float64) - ref0).max() / np.abs(ref0).max())
+        parity = {"status": "ok" if err < 1e-2 else "FAIL", "max_rel_err": err,
+                  "bar": 1e-2, "checked": "image 0 of rank 0's shard, embeddings of the "
+                                          "last graph replay against the oracle's replay "
+                                          "of the unfused plan (oracle/executor.py)"}
 
     if rank == 0:
         line = {
@@ -443,13 +507,10 @@ def run_b200(args) -> None:
                             f"global batch {args.batch}, sharded by image",
                 "image_size": cfg.image_size, "global_batch": args.batch,
                 "seq_len": cfg.num_tokens, "parallelism": f"image-sharded x{world}",
-                "weights": args.weights, "plan_ops": plan.n_ops, "fusions": {"attention": use_att, "qkv_rope": use_qkv,
-                                                   "rope": args.rope if use_qkv else None,
-                                                   "ln_fold": args.ln_fold == "on",
-                                                   "patch_cast": not args.no_patch_cast,
-                                                   "residual": not args.no_residual_fusion},
+                "weights": args.weights, "plan_ops": plan.n_ops,
+                "fusions": {k: bool(v) for k, v in rewrites.items()},
                 "l2": f"inputs larger than L2: each step reads {plan.const_bytes / 1e6:.0f} MB "
-                      f"of consts and {n * 6.29:.0f} MB of images per GPU",
+                      f"of consts and {host_in.numel() * 4 / 1e6:.0f} MB of images per GPU",
             },
             "e2e": {"value": e2e, "unit": UNIT,
                     "h2d_bytes_per_step": int(host_in.numel() * 4),
@@ -458,9 +519,19 @@ def run_b200(args) -> None:
             "roofline": {"kernel": dname, "bound": dbound, "achieved": achieved,
                          "peak": peak, "unit": punit, "frac": achieved / peak,
                          "peak_source": f"{pk['src']} "
-                                        f"({'sustained bf16' if dbound == 'tensor' else 'hbm copy'})",
+                                        f"({'burst bf16' if dbound == 'tensor' else 'hbm copy'}; "
+                                        f"each op timed alone)",
+                         "algorithmic": dflops if dbound == "tensor" else dbytes,
+                         "algorithmic_unit": "FLOP per launch" if dbound == "tensor"
+                                             else "bytes per launch",
                          "traffic": traffic, "traffic_unit": "bytes per launch (dram read + write)",
-                         "traffic_source": traffic_note, "share": dom_ns / total_ns},
+                         "traffic_source": traffic_note, "share": dom_ns / total_ns,
+                         "encoder_frac": (roof_s * 1e3) / (ms_max / args.steps),
+                         "encoder_frac_note": "sum over the step's kernels of max(FLOPs / burst "
+                                              "tensor peak, bytes / HBM copy bandwidth), over "
+                                              "the device-timed ms per step"},
+            "gather_ms_per_step": gather_ms,
+            "parity": parity,
             "kernels": kernels[:8],
             "clocks": clk,
             "cpu_baseline": cpu,

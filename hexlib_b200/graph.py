@@ -764,6 +764,14 @@ def _apply_rewrites(g: Graph, attention: bool, residual: bool, qkv: bool,
     return g, derived
 
 
+# The CUDA-only rewrites the encoder runs with unless told otherwise -- the
+# plan bench.py measures: fused attention over one packed q/k/v projection
+# with RoPE in that GEMM's epilogue, residual adds in the GEMM epilogues,
+# patchify writing fp16 rows. (`ln_fold` stays off: measured slower.)
+DEFAULT_REWRITES = MappingProxyType({"attention": True, "qkv": True, "rope_epilogue": True,
+                                     "residual": True, "patch_cast": True})
+
+
 def compile_for_cuda(graph: Graph, attention: bool = False, residual: bool = False,
                      qkv: bool = False, rope_epilogue: bool = False,
                      ln_fold: bool = False, patch_cast: bool = False) -> ExecPlan:

@@ -43,8 +43,18 @@ def test_gemm_is_the_same_in_either_order(M, K, N, act):
     assert np.array_equal(y0.view(np.uint16), y1.view(np.uint16))
 
 
-def test_residual_gemm_is_the_same_in_either_order():
-    M, K, N = 20000, 768, 768
+@pytest.mark.parametrize("M,K,N", [
+    (20000, 768, 768),      # partial last pair tile
+    (65536, 768, 768),      # the o-projection of the 512^2 x 64 encoder: 768 pair tiles,
+                            # both TMEM accumulators cycling, next-tile residual prefetch (K <= 1024)
+    (65536, 3072, 768),     # its fc2: K > 1024, no prefetch
+])
+def test_residual_gemm_matches_the_oracle_in_either_order(M, K, N):
+    """At the encoder's own row counts each CTA pair runs many tiles; both
+    orders must equal each other bit for bit and the unfused oracle chain
+    (matmul_epilogue rounded to fp16, then the residual add) within the bar."""
+    from oracle import executor
+    from tests.tolerance import assert_close_f16
     a, w, r = r16((M, K), 4), r16((K, N), 5, 0.03), r16((M, N), 6)
     bias = (np.random.default_rng(7).standard_normal(N) * 0.02).astype(np.float32)
     da, dw, db, dr = U.dev(a), U.dev(w), U.dev(bias), U.dev(r)
@@ -55,6 +65,9 @@ def test_residual_gemm_is_the_same_in_either_order():
                U.ptr(dr), U.ptr(y), M, K, N, 0, U.stream())
         return y
     y0, y1 = twice(run)
+    ref = executor.matmul_epilogue_residual_chain(
+        a.astype(np.float32), w.astype(np.float32), bias, r.astype(np.float32))
+    assert_close_f16(y0, ref, what=f"residual GEMM {M}x{K}x{N}")
     assert np.array_equal(y0.view(np.uint16), y1.view(np.uint16))
 
 
