@@ -1,57 +1,71 @@
-"""The graph the CUDA path executes: IR, the vision-encoder builder, fusion,
-and the rewrites only this backend performs.
+"""The graph the CUDA path executes: a small IR, the vision encoder written as
+a program text for it, the matmul-epilogue fusion, and the rewrites only this
+backend performs.
 
 The reference's graph compiler is the contract this backend consumes -- its
-`Compiled(graph, plan)` is accepted as is by `wholeplan.build_cuda_plan` --
-but it is not importable where the backend runs, so the part of it that
-decides WHAT executes is restated here, producing the same post-fusion graph
-(same tensor names, shapes, dtypes, op ids, kinds and attrs; checked against
-the reference by tests/test_graph_matches_reference.py):
+`Compiled(graph, plan)` is accepted as is by `wholeplan.build_cuda_plan`, and
+its JSON artefact by `from_compiled_json` -- but it is not importable where
+the backend runs, so this module produces the same post-fusion graph on its
+own: the same tensor names, shapes, dtypes and const flags, op ids, kinds,
+inputs, outputs and attrs as hexlib/models/vit.py:113-218 after
+hexlib/graph/fuse.py:16-92 (checked against the reference's own plans by
+tests/test_graph_matches_reference.py). Those names, ids and attrs are the
+interface -- feeds, plans and blobs key on them -- so they are reproduced
+exactly; how they are produced is this module's own:
 
-  * `Tensor`, `Op`, `Graph`                    hexlib/graph/ir.py:78-225
-  * `VitConfig`, `build_vision_encoder`        hexlib/models/vit.py:17-218
-  * `QWEN35_08B_VISION`, `qwen35_at`           hexlib/models/qwen35.py:15-52
-  * `fuse` (matmul + bias add (+ GELU))        hexlib/graph/fuse.py:16-92
-  * `compile_for_cuda` -> `ExecPlan`           the executable half of
-                                               hexlib/graph/pipeline.py:59-150
+  * the encoder is data: three op programs (stem, block, merger) in a line
+    format parsed by `_Program` -- one op per line, consts declared where
+    they are first read, shapes and attrs in symbols of the configuration;
+  * every graph rewrite, the reference's fusion included, is a set of edits
+    recorded on an `_Edit` (replace an op in place, drop ops and tensors, add
+    tensors) and applied in one step.
 
-VTCM allocation and DMA insertion are NOT restated: on the GPU the arena is
+VTCM allocation and DMA insertion are not produced: on the GPU the arena is
 laid out by `wholeplan`, and tiles move by TMA inside the kernels.
 
-CUDA-ONLY REWRITES (`fuse_attention`, `fuse_residual`) turn chains of plan
-ops into the appended wire kinds `attention` and `matmul_epilogue_residual`.
-They change which kernels run and how many intermediates are written, not
-the function computed; tests compare both forms against the oracle.
+CUDA-ONLY REWRITES (`fuse_attention`, `fuse_residual`, `fuse_qkv`,
+`fuse_patchify_cast`, `fold_layernorm`) turn chains of plan ops into the
+appended wire kinds. They change which kernels run and how many
+intermediates are written, not the function computed; tests compare both
+forms against the oracle.
 """
 from __future__ import annotations
 
+import ast
 import dataclasses
 import json
-import math
+import re
 from dataclasses import dataclass, field
 from types import MappingProxyType
-from typing import Any, Mapping
+from typing import Any, Iterable, Mapping
+
+from hexlib_b200 import quant as _quant
 
 DTYPES = frozenset({"fp32", "fp16", "int32", "q4_0", "q8_0"})
-_DENSE_BYTES = {"fp32": 4, "fp16": 2, "int32": 4}
-_BLOCK = {"q4_0": (32, 18), "q8_0": (32, 34)}
+_ITEM_BYTES = {"fp32": 4, "fp16": 2, "int32": 4}
 
 
 def nbytes(shape: tuple[int, ...], dtype: str) -> int:
-    """Bytes of a tensor (ir.py:40-56): dense, or 32-element quantized blocks."""
-    n = math.prod(shape) if shape else 1
-    if dtype in _BLOCK:
-        blk, blk_bytes = _BLOCK[dtype]
-        if not shape or shape[-1] % blk:
-            raise ValueError(f"{dtype} tensor {shape} needs a last dim multiple of {blk}")
-        return n // blk * blk_bytes
-    if dtype not in _DENSE_BYTES:
-        raise ValueError(f"unknown dtype {dtype!r}")
-    return n * _DENSE_BYTES[dtype]
+    """Storage bytes of a tensor: dense element bytes, or 32-element blocks of
+    18 (q4_0) / 34 (q8_0) bytes along the last axis (hexlib/graph/ir.py:23-56)."""
+    if dtype in _quant.BLOCK_BYTES:
+        return _quant.nbytes(tuple(shape), dtype)
+    try:
+        item = _ITEM_BYTES[dtype]
+    except KeyError:
+        raise ValueError(f"unknown dtype {dtype!r}") from None
+    count = 1
+    for d in shape:
+        count *= int(d)
+    return count * item
 
+
+# ---- IR ------------------------------------------------------------------------------
 
 @dataclass(frozen=True)
 class Tensor:
+    """A named value: graph input, intermediate, or const (a weight or table
+    fed once per session)."""
     name: str
     dtype: str
     shape: tuple[int, ...]
@@ -62,8 +76,13 @@ class Tensor:
         return nbytes(self.shape, self.dtype)
 
 
+def _frozen(attrs: Mapping[str, Any]) -> Mapping[str, Any]:
+    return MappingProxyType(dict(attrs))
+
+
 @dataclass(frozen=True)
 class Op:
+    """One step: `kind` reads `inputs` and writes `outputs` (tensor names)."""
     id: int
     kind: str
     inputs: tuple[str, ...]
@@ -73,18 +92,22 @@ class Op:
     def __post_init__(self) -> None:
         object.__setattr__(self, "inputs", tuple(self.inputs))
         object.__setattr__(self, "outputs", tuple(self.outputs))
-        object.__setattr__(self, "attrs", MappingProxyType(dict(self.attrs)))
+        object.__setattr__(self, "attrs", _frozen(self.attrs))
+
+    def with_(self, **changes) -> "Op":
+        return dataclasses.replace(self, **changes)
 
 
 @dataclass(frozen=True)
 class Graph:
+    """Tensors by name, ops in execution order, graph inputs and outputs."""
     tensors: Mapping[str, Tensor]
     ops: tuple[Op, ...]
     inputs: tuple[str, ...]
     outputs: tuple[str, ...]
 
     def __post_init__(self) -> None:
-        object.__setattr__(self, "tensors", MappingProxyType(dict(self.tensors)))
+        object.__setattr__(self, "tensors", _frozen(self.tensors))
         object.__setattr__(self, "ops", tuple(self.ops))
         object.__setattr__(self, "inputs", tuple(self.inputs))
         object.__setattr__(self, "outputs", tuple(self.outputs))
@@ -93,41 +116,45 @@ class Graph:
         return self.tensors[name]
 
     def problems(self) -> list[str]:
-        """Structural problems (ir.py:164-225), as text; empty means valid."""
-        out: list[str] = []
+        """Why this graph cannot run in its op order (empty when it can): an
+        empty graph, an unknown name, a read before any write, a second
+        write, a duplicate op id, an output nobody writes. The checks of
+        hexlib/graph/ir.py:164-225, as a replay of the op order."""
+        issues: list[str] = []
         if not self.ops:
-            out.append("graph has no ops")
+            issues.append("the graph has no ops")
         if not self.outputs:
-            out.append("graph declares no outputs")
-        written = set(self.inputs) | {n for n, t in self.tensors.items() if t.const}
-        seen: set[int] = set()
+            issues.append("the graph names no outputs")
+        ready = {n for n, t in self.tensors.items() if t.const}
+        ready.update(self.inputs)
+        ids: set[int] = set()
         for op in self.ops:
-            if op.id in seen:
-                out.append(f"duplicate op id {op.id}")
-            seen.add(op.id)
-            for n in op.inputs:
-                if n not in self.tensors:
-                    out.append(f"op {op.id} ({op.kind}) reads undeclared {n!r}")
-                elif n not in written:
-                    out.append(f"op {op.id} ({op.kind}) reads {n!r} before it is written")
-            for n in op.outputs:
-                if n not in self.tensors:
-                    out.append(f"op {op.id} ({op.kind}) writes undeclared {n!r}")
-                elif n in written:
-                    out.append(f"tensor {n!r} is written twice (op {op.id})")
-                else:
-                    written.add(n)
-        for n in self.outputs:
-            if n not in written:
-                out.append(f"graph output {n!r} is never written")
-        return out
+            where = f"op {op.id} ({op.kind})"
+            if op.id in ids:
+                issues.append(f"{where}: its id is used twice")
+            ids.add(op.id)
+            for name in op.inputs:
+                if name not in self.tensors:
+                    issues.append(f"{where}: reads {name!r}, which is not declared")
+                elif name not in ready:
+                    issues.append(f"{where}: reads {name!r} before anything writes it")
+            for name in op.outputs:
+                if name not in self.tensors:
+                    issues.append(f"{where}: writes {name!r}, which is not declared")
+                elif name in ready:
+                    issues.append(f"{where}: writes {name!r}, which already has a value")
+                ready.add(name)
+        issues.extend(f"graph output {n!r}: nothing writes it"
+                      for n in self.outputs if n not in ready)
+        return issues
 
 
-# ---- the model ---------------------------------------------------------------
+# ---- the model: configuration ---------------------------------------------------------
 
 @dataclass(frozen=True)
 class VitConfig:
-    """vit.py:17-48."""
+    """The vision tower's hyper-parameters, with the field names of
+    hexlib/models/vit.py:17-48 (the reference's configs are built from them)."""
     depth: int
     hidden_size: int
     num_heads: int
@@ -145,24 +172,22 @@ class VitConfig:
 
     @property
     def grid(self) -> int:
+        """Patches along each side of the image."""
         return self.image_size // self.patch_size
 
     @property
     def num_tokens(self) -> int:
-        return self.grid * self.grid
+        return self.grid ** 2
 
     @property
     def head_dim(self) -> int:
         return self.hidden_size // self.num_heads
 
-    @property
-    def merge_unit(self) -> int:
-        return self.spatial_merge_size ** 2
 
-
-# qwen35.py:15-42 -- the Qwen3.5-0.8B vision tower. The reference ships it
-# with q4_0 weights for the DSP; this backend's configurations use fp16
-# weights (weight_dtype="fp16"), the variant `qwen35_at` + replace produces.
+# The Qwen3.5-0.8B vision tower (hexlib/models/qwen35.py:15-42): 12 blocks of
+# width 768 with 12 heads, MLP 3072, 16x16 patches over 2 frames, 2x2 merge
+# to 1024 outputs. The reference ships it with q4_0 weights for the DSP; this
+# backend's configurations use fp16 weights (`qwen35_at`'s default).
 QWEN35_08B_VISION = VitConfig(
     depth=12, hidden_size=768, num_heads=12, intermediate_size=3072,
     patch_size=16, temporal_patch_size=2, in_channels=3, spatial_merge_size=2,
@@ -173,326 +198,404 @@ QWEN35_08B_VISION = VitConfig(
 
 def qwen35_at(image_size: int, weight_dtype: str = "fp16",
               act_dtype: str = "fp16") -> VitConfig:
-    """The tower at another square resolution (qwen35.py:45-52), fp16 weights
-    by default."""
+    """The tower at another square resolution (hexlib/models/qwen35.py:45-52),
+    fp16 weights unless asked otherwise."""
     return dataclasses.replace(QWEN35_08B_VISION, image_size=image_size,
                                weight_dtype=weight_dtype, act_dtype=act_dtype)
 
 
 def config_problems(cfg: VitConfig) -> list[str]:
-    """vit.py:247-283."""
-    out = []
-    for f in dataclasses.fields(VitConfig):
-        v = getattr(cfg, f.name)
-        if isinstance(v, int) and not isinstance(v, bool) and v <= 0:
-            out.append(f"{f.name} {v} must be positive")
-    if out:
-        return out
+    """Why `cfg` cannot describe an encoder (empty when it can): every count
+    positive, whole patches, a patch grid the merge divides, whole heads of
+    even width (the rotation pairs dimensions) -- the conditions of
+    hexlib/models/vit.py:247-283."""
+    counts = ("depth", "hidden_size", "num_heads", "intermediate_size", "patch_size",
+              "temporal_patch_size", "in_channels", "spatial_merge_size",
+              "out_hidden_size", "image_size")
+    bad = [f"{k} must be a positive integer, not {getattr(cfg, k)!r}"
+           for k in counts if not isinstance(getattr(cfg, k), int) or getattr(cfg, k) <= 0]
+    if bad:
+        return bad
     if cfg.image_size % cfg.patch_size:
-        out.append(f"image_size {cfg.image_size} is not divisible by patch_size {cfg.patch_size}")
+        bad.append(f"a {cfg.image_size}-pixel image is not a whole number of "
+                   f"{cfg.patch_size}-pixel patches")
     elif cfg.grid % cfg.spatial_merge_size:
-        out.append(f"patch grid {cfg.grid} is not divisible by spatial_merge_size")
+        bad.append(f"the {cfg.grid}-patch grid does not split into "
+                   f"{cfg.spatial_merge_size}x{cfg.spatial_merge_size} merge blocks")
     if cfg.hidden_size % cfg.num_heads:
-        out.append("hidden_size is not divisible by num_heads")
+        bad.append(f"width {cfg.hidden_size} does not split into {cfg.num_heads} heads")
     elif cfg.head_dim % 2:
-        out.append("head_dim must be even for 2D RoPE")
-    return out
+        bad.append(f"head width {cfg.head_dim} is odd; the 2-D rotation needs pairs")
+    return bad
 
 
-class _Builder:
+# ---- the model: op programs -----------------------------------------------------------
+#
+# One op per line:   OUT[:dtype] = KIND(ARG, ARG, ...) [SHAPE] key=value ...
+#   ARG is a tensor name, or `$name:dtype[SHAPE]` for a const, declared where
+#   it is first read (a later `$` of the same name must agree). dtype `w` is
+#   the configuration's weight dtype, `act` its activation dtype (the default
+#   for outputs). SHAPE and attr values use the symbols `_symbols` defines;
+#   `{b}` and `{x}` are the block prefix and the residual stream's tensor.
+
+STEM = """
+patches:fp32        = patchify(image) [T,PF] patch=PATCH temporal_patch=TPATCH merge=MERGE grid_h=GRID grid_w=GRID
+patches.cast        = cast(patches) [T,PF] dtype=ACT
+patch_embed.out.mm  = matmul(patches.cast, $w_patch_embed:w[PF,C]) [T,C]
+patch_embed.out     = add(patch_embed.out.mm, $b_patch_embed:fp32[C]) [T,C]
+x0                  = add(patch_embed.out, $pos_embed:fp32[T,C]) [T,C]
+"""
+
+# A pre-LayerNorm block: q/k/v projections, 2-D RoPE on q and k, attention as
+# scale -> QK^T -> softmax -> PV over [H, T, D] heads, output projection and
+# residual, then LayerNorm -> fc1 -> GELU(tanh) -> fc2 and residual.
+BLOCK = """
+{b}.ln1.out    = layernorm({x}, ${b}.ln1_w:fp32[C], ${b}.ln1_b:fp32[C]) [T,C] eps=EPS
+{b}.q.out.mm   = matmul({b}.ln1.out, ${b}.wq:w[C,C]) [T,C]
+{b}.q.out      = add({b}.q.out.mm, ${b}.bq:fp32[C]) [T,C]
+{b}.q.h        = reshape({b}.q.out) [T,H,D] shape=(T,H,D)
+{b}.q.rope     = rope_2d({b}.q.h, $rope_cos:fp32[T,D], $rope_sin:fp32[T,D]) [T,H,D]
+{b}.q.t        = transpose({b}.q.rope) [H,T,D] perm=(1,0,2)
+{b}.k.out.mm   = matmul({b}.ln1.out, ${b}.wk:w[C,C]) [T,C]
+{b}.k.out      = add({b}.k.out.mm, ${b}.bk:fp32[C]) [T,C]
+{b}.k.h        = reshape({b}.k.out) [T,H,D] shape=(T,H,D)
+{b}.k.rope     = rope_2d({b}.k.h, rope_cos, rope_sin) [T,H,D]
+{b}.k.t        = transpose({b}.k.rope) [H,T,D] perm=(1,0,2)
+{b}.v.out.mm   = matmul({b}.ln1.out, ${b}.wv:w[C,C]) [T,C]
+{b}.v.out      = add({b}.v.out.mm, ${b}.bv:fp32[C]) [T,C]
+{b}.v.h        = reshape({b}.v.out) [T,H,D] shape=(T,H,D)
+{b}.v.t        = transpose({b}.v.h) [H,T,D] perm=(1,0,2)
+{b}.q.scaled   = scale({b}.q.t) [H,T,D] factor=QK_SCALE
+{b}.k.tt       = transpose({b}.k.t) [H,D,T] perm=(0,2,1)
+{b}.scores     = matmul({b}.q.scaled, {b}.k.tt) [H,T,T]
+{b}.probs      = softmax({b}.scores) [H,T,T] axis=-1
+{b}.ctx        = matmul({b}.probs, {b}.v.t) [H,T,D]
+{b}.ctx.t      = transpose({b}.ctx) [T,H,D] perm=(1,0,2)
+{b}.ctx.f      = reshape({b}.ctx.t) [T,C] shape=(T,C)
+{b}.o.out.mm   = matmul({b}.ctx.f, ${b}.wo:w[C,C]) [T,C]
+{b}.o.out      = add({b}.o.out.mm, ${b}.bo:fp32[C]) [T,C]
+{b}.resid1     = add({x}, {b}.o.out) [T,C]
+{b}.ln2.out    = layernorm({b}.resid1, ${b}.ln2_w:fp32[C], ${b}.ln2_b:fp32[C]) [T,C] eps=EPS
+{b}.fc1.out.mm = matmul({b}.ln2.out, ${b}.w_fc1:w[C,FF]) [T,FF]
+{b}.fc1.out    = add({b}.fc1.out.mm, ${b}.b_fc1:fp32[FF]) [T,FF]
+{b}.act        = gelu_tanh({b}.fc1.out) [T,FF]
+{b}.fc2.out.mm = matmul({b}.act, ${b}.w_fc2:w[FF,C]) [T,C]
+{b}.fc2.out    = add({b}.fc2.out.mm, ${b}.b_fc2:fp32[C]) [T,C]
+{b}.resid2     = add({b}.resid1, {b}.fc2.out) [T,C]
+"""
+
+# The patch merger: LayerNorm, each 2x2 block of tokens concatenated into one
+# row (tokens are already in merge-block order), GELU(erf) MLP to the output width.
+MERGER = """
+merger.ln.out     = layernorm({x}, $m_ln_w:fp32[C], $m_ln_b:fp32[C]) [T,C] eps=EPS
+merger.concat     = reshape(merger.ln.out) [TM,CM] shape=(TM,CM)
+merger.fc1.out.mm = matmul(merger.concat, $w_m1:w[CM,CM]) [TM,CM]
+merger.fc1.out    = add(merger.fc1.out.mm, $b_m1:fp32[CM]) [TM,CM]
+merger.act        = gelu_erf(merger.fc1.out) [TM,CM]
+merger.out.mm     = matmul(merger.act, $w_m2:w[CM,OUT]) [TM,OUT]
+merger.out        = add(merger.out.mm, $b_m2:fp32[OUT]) [TM,OUT]
+"""
+
+
+def _symbols(cfg: VitConfig) -> dict[str, Any]:
+    merged = cfg.spatial_merge_size ** 2
+    return {
+        "T": cfg.num_tokens, "C": cfg.hidden_size, "H": cfg.num_heads, "D": cfg.head_dim,
+        "FF": cfg.intermediate_size, "OUT": cfg.out_hidden_size,
+        "PF": cfg.in_channels * cfg.temporal_patch_size * cfg.patch_size ** 2,
+        "TM": cfg.num_tokens // merged, "CM": cfg.hidden_size * merged,
+        "PATCH": cfg.patch_size, "TPATCH": cfg.temporal_patch_size,
+        "MERGE": cfg.spatial_merge_size, "GRID": cfg.grid,
+        "EPS": cfg.layernorm_eps, "QK_SCALE": float(cfg.head_dim) ** -0.5,
+        "ACT": cfg.act_dtype,
+    }
+
+
+_LINE = re.compile(r"^(?P<out>[^\s=:]+)(?::(?P<dt>\w+))?\s*=\s*(?P<kind>\w+)\((?P<args>[^)]*)\)"
+                   r"\s*\[(?P<shape>[^\]]*)\]\s*(?P<attrs>.*)$")
+_CONST = re.compile(r"^\$(?P<name>[^:]+):(?P<dt>\w+)\[(?P<shape>[^\]]*)\]$")
+
+
+class _Program:
+    """Assembles op programs into one graph: op ids in emission order."""
+
     def __init__(self, cfg: VitConfig) -> None:
-        self.cfg = cfg
+        self.sym = _symbols(cfg)
+        self.dtypes = {"w": cfg.weight_dtype, "act": cfg.act_dtype, "fp32": "fp32",
+                       "fp16": "fp16", "int32": "int32"}
         self.tensors: dict[str, Tensor] = {}
         self.ops: list[Op] = []
 
-    def declare(self, name, shape, dtype, const=False) -> str:
-        if name in self.tensors:
-            raise ValueError(f"tensor {name!r} declared twice")
-        self.tensors[name] = Tensor(name, dtype, tuple(shape), const)
-        return name
+    def _value(self, text: str) -> Any:
+        text = text.strip()
+        if text.startswith("("):
+            return tuple(self._value(p) for p in text[1:-1].split(","))
+        if text in self.sym:
+            return self.sym[text]
+        return ast.literal_eval(text)
 
-    def const(self, name, shape, dtype=None) -> str:
-        return self.declare(name, shape, dtype or self.cfg.weight_dtype, const=True)
+    def _shape(self, text: str) -> tuple[int, ...]:
+        return tuple(int(self._value(p)) for p in text.split(",")) if text.strip() else ()
 
-    def emit(self, kind, inputs, out, shape, attrs=None, dtype=None) -> str:
-        self.declare(out, shape, dtype or self.cfg.act_dtype)
-        self.ops.append(Op(len(self.ops), kind, tuple(inputs), (out,), attrs or {}))
-        return out
+    def _declare(self, t: Tensor) -> str:
+        have = self.tensors.get(t.name)
+        if have is not None and have != t:
+            raise ValueError(f"{t.name!r} declared as {have} and as {t}")
+        self.tensors[t.name] = t
+        return t.name
 
-    def linear(self, x, wname, bname, k, n, out) -> str:
-        """matmul + bias add, weight [k, n], bias fp32 (vit.py:91-96)."""
-        w = self.const(wname, (k, n))
-        b = self.const(bname, (n,), "fp32")
-        rows = self.tensors[x].shape[:-1]
-        h = self.emit("matmul", (x, w), f"{out}.mm", rows + (n,))
-        return self.emit("add", (h, b), out, rows + (n,))
+    def _arg(self, text: str) -> str:
+        m = _CONST.match(text)
+        if m is None:
+            if text not in self.tensors:
+                raise ValueError(f"{text!r} is read before it is declared")
+            return text
+        return self._declare(Tensor(m["name"], self.dtypes[m["dt"]], self._shape(m["shape"]),
+                                    True))
 
-    def layernorm(self, x, wname, bname, out, shape, eps) -> str:
-        w = self.const(wname, (shape[-1],), "fp32")
-        b = self.const(bname, (shape[-1],), "fp32")
-        return self.emit("layernorm", (x, w, b), out, shape, {"eps": eps})
+    @staticmethod
+    def _split(text: str) -> list[str]:
+        """Split on the commas outside [...]."""
+        parts, depth, cur = [], 0, ""
+        for ch in text:
+            depth += (ch == "[") - (ch == "]")
+            if ch == "," and depth == 0:
+                parts.append(cur.strip())
+                cur = ""
+            else:
+                cur += ch
+        return parts + [cur.strip()]
+
+    def declare_input(self, name: str, dtype: str, shape: tuple[int, ...]) -> None:
+        self._declare(Tensor(name, dtype, tuple(shape)))
+
+    def run(self, program: str, **names: str) -> None:
+        for raw in program.strip().splitlines():
+            line = raw.format(**names)
+            m = _LINE.match(line.strip())
+            if m is None:
+                raise ValueError(f"cannot parse op line {line!r}")
+            ins = tuple(self._arg(a) for a in self._split(m["args"]))
+            out = m["out"]
+            if out in self.tensors:
+                raise ValueError(f"{out!r} is written twice")
+            self._declare(Tensor(out, self.dtypes[m["dt"] or "act"], self._shape(m["shape"])))
+            attrs = {}
+            for item in m["attrs"].split():
+                key, val = item.split("=", 1)
+                attrs[key] = self._value(val)
+            self.ops.append(Op(len(self.ops), m["kind"], ins, (out,), attrs))
+
+    def graph(self, inputs: tuple[str, ...], outputs: tuple[str, ...]) -> Graph:
+        return Graph(self.tensors, tuple(self.ops), inputs, outputs)
 
 
 def build_vision_encoder(cfg: VitConfig) -> Graph:
-    """The encoder graph (vit.py:113-218): patchify, cast, patch embed,
-    + pos_embed, `depth` pre-LayerNorm blocks with 2D RoPE attention and a
-    GELU-tanh MLP, then the 2x2 merger (LayerNorm, reshape, GELU-erf MLP)."""
-    problems = config_problems(cfg)
-    if problems:
-        raise ValueError("invalid vision config: " + "; ".join(problems))
-    b = _Builder(cfg)
-    n, H = cfg.num_tokens, cfg.hidden_size
-    heads, d = cfg.num_heads, cfg.head_dim
-    merge = cfg.spatial_merge_size
-    feat = cfg.in_channels * cfg.temporal_patch_size * cfg.patch_size ** 2
-
-    image = b.declare("image", (cfg.in_channels, cfg.temporal_patch_size,
-                                cfg.image_size, cfg.image_size), "fp32")
-    patches = b.emit("patchify", (image,), "patches", (n, feat), {
-        "patch": cfg.patch_size, "temporal_patch": cfg.temporal_patch_size,
-        "merge": merge, "grid_h": cfg.grid, "grid_w": cfg.grid}, dtype="fp32")
-    pc = b.emit("cast", (patches,), "patches.cast", (n, feat),
-                {"dtype": cfg.act_dtype}, dtype=cfg.act_dtype)
-    emb = b.linear(pc, "w_patch_embed", "b_patch_embed", feat, H, "patch_embed.out")
-    pos = b.const("pos_embed", (n, H), "fp32")
-    x = b.emit("add", (emb, pos), "x0", (n, H))
-    cos = b.const("rope_cos", (n, d), "fp32")
-    sin = b.const("rope_sin", (n, d), "fp32")
-
-    for layer in range(cfg.depth):
-        p = f"blk{layer}"
-        a = b.layernorm(x, f"{p}.ln1_w", f"{p}.ln1_b", f"{p}.ln1.out", (n, H),
-                        cfg.layernorm_eps)
-        t = {}
-        for which in ("q", "k", "v"):
-            proj = b.linear(a, f"{p}.w{which}", f"{p}.b{which}", H, H, f"{p}.{which}.out")
-            hd = b.emit("reshape", (proj,), f"{p}.{which}.h", (n, heads, d),
-                        {"shape": (n, heads, d)})
-            if which in ("q", "k"):
-                hd = b.emit("rope_2d", (hd, cos, sin), f"{p}.{which}.rope", (n, heads, d))
-            t[which] = b.emit("transpose", (hd,), f"{p}.{which}.t", (heads, n, d),
-                              {"perm": (1, 0, 2)})
-        qs = b.emit("scale", (t["q"],), f"{p}.q.scaled", (heads, n, d),
-                    {"factor": float(d) ** -0.5})
-        ktt = b.emit("transpose", (t["k"],), f"{p}.k.tt", (heads, d, n), {"perm": (0, 2, 1)})
-        s = b.emit("matmul", (qs, ktt), f"{p}.scores", (heads, n, n))
-        pr = b.emit("softmax", (s,), f"{p}.probs", (heads, n, n), {"axis": -1})
-        ctx = b.emit("matmul", (pr, t["v"]), f"{p}.ctx", (heads, n, d))
-        ctxt = b.emit("transpose", (ctx,), f"{p}.ctx.t", (n, heads, d), {"perm": (1, 0, 2)})
-        ctxf = b.emit("reshape", (ctxt,), f"{p}.ctx.f", (n, H), {"shape": (n, H)})
-        proj = b.linear(ctxf, f"{p}.wo", f"{p}.bo", H, H, f"{p}.o.out")
-        xa = b.emit("add", (x, proj), f"{p}.resid1", (n, H))
-        c = b.layernorm(xa, f"{p}.ln2_w", f"{p}.ln2_b", f"{p}.ln2.out", (n, H),
-                        cfg.layernorm_eps)
-        f1 = b.linear(c, f"{p}.w_fc1", f"{p}.b_fc1", H, cfg.intermediate_size, f"{p}.fc1.out")
-        g = b.emit("gelu_tanh", (f1,), f"{p}.act", (n, cfg.intermediate_size))
-        f2 = b.linear(g, f"{p}.w_fc2", f"{p}.b_fc2", cfg.intermediate_size, H, f"{p}.fc2.out")
-        x = b.emit("add", (xa, f2), f"{p}.resid2", (n, H))
-
-    M = H * cfg.merge_unit
-    mn = b.layernorm(x, "m_ln_w", "m_ln_b", "merger.ln.out", (n, H), cfg.layernorm_eps)
-    mc = b.emit("reshape", (mn,), "merger.concat", (n // cfg.merge_unit, M),
-                {"shape": (n // cfg.merge_unit, M)})
-    m1 = b.linear(mc, "w_m1", "b_m1", M, M, "merger.fc1.out")
-    mg = b.emit("gelu_erf", (m1,), "merger.act", (n // cfg.merge_unit, M))
-    out = b.linear(mg, "w_m2", "b_m2", M, cfg.out_hidden_size, "merger.out")
-    return Graph(b.tensors, tuple(b.ops), (image,), (out,))
+    """The encoder graph of hexlib/models/vit.py:113-218 for `cfg`: the image
+    [channels, frames, S, S] fp32 in, the merged embeddings out."""
+    bad = config_problems(cfg)
+    if bad:
+        raise ValueError("invalid vision config: " + "; ".join(bad))
+    p = _Program(cfg)
+    p.declare_input("image", "fp32", (cfg.in_channels, cfg.temporal_patch_size,
+                                      cfg.image_size, cfg.image_size))
+    p.run(STEM)
+    stream = "x0"
+    for i in range(cfg.depth):
+        p.run(BLOCK, b=f"blk{i}", x=stream)
+        stream = f"blk{i}.resid2"
+    p.run(MERGER, x=stream)
+    return p.graph(("image",), ("merger.out",))
 
 
 def weight_names(cfg: VitConfig) -> tuple[str, ...]:
-    """Every const the graph needs, sorted (vit.py:99-110)."""
+    """Every const the encoder reads, sorted (the order feeds are drawn in)."""
     g = build_vision_encoder(cfg)
     return tuple(sorted(n for n, t in g.tensors.items() if t.const))
 
 
-# ---- passes ------------------------------------------------------------------------
+# ---- graph edits ----------------------------------------------------------------------
+
+class _Edit:
+    """The edits of one rewrite pass over `graph`, applied together by
+    `result()`: ops replaced in place (a replacement keeps the position of the
+    op it replaces), ops removed, tensors removed or added."""
+
+    def __init__(self, graph: Graph) -> None:
+        self.graph = graph
+        self.readers: dict[str, list[Op]] = {}
+        for op in graph.ops:
+            for n in op.inputs:
+                self.readers.setdefault(n, []).append(op)
+        self.writer = {n: op for op in graph.ops for n in op.outputs}
+        self.kept_outputs = frozenset(graph.outputs)
+        self.replaced: dict[int, Op] = {}
+        self.removed: set[int] = set()
+        self.dead: set[str] = set()
+        self.born: dict[str, Tensor] = {}
+
+    def only_reader(self, name: str) -> Op | None:
+        """The one op that reads `name`, if exactly one does and `name` is
+        not a graph output (so it may disappear)."""
+        r = self.readers.get(name, [])
+        return r[0] if len(r) == 1 and name not in self.kept_outputs else None
+
+    def written_by(self, name: str, kind: str) -> Op | None:
+        op = self.writer.get(name)
+        return op if op is not None and op.kind == kind else None
+
+    def touched(self, op: Op) -> bool:
+        return op.id in self.removed or op.id in self.replaced
+
+    def replace(self, op: Op, new: Op) -> None:
+        self.replaced[op.id] = new
+
+    def remove(self, ops: Iterable[Op], tensors: Iterable[str] = ()) -> None:
+        for op in ops:
+            self.removed.add(op.id)
+        self.dead.update(tensors)
+
+    def add_tensor(self, t: Tensor) -> str:
+        self.born[t.name] = t
+        return t.name
+
+    def result(self, prune_consts: bool = False) -> Graph:
+        if not self.replaced and not self.removed:
+            return self.graph
+        ops = tuple(self.replaced.get(o.id, o) for o in self.graph.ops
+                    if o.id in self.replaced or o.id not in self.removed)
+        tensors = {n: t for n, t in self.graph.tensors.items() if n not in self.dead}
+        tensors.update(self.born)
+        if prune_consts:
+            read = {n for o in ops for n in o.inputs}
+            tensors = {n: t for n, t in tensors.items() if not t.const or n in read}
+        return Graph(tensors, ops, self.graph.inputs, self.graph.outputs)
+
+
+# ---- the reference's fusion -----------------------------------------------------------
 
 FUSABLE_ACTS = ("gelu_tanh", "gelu_erf")
 
 
-def _consumers(graph: Graph) -> dict[str, list[Op]]:
-    out: dict[str, list[Op]] = {}
-    for op in graph.ops:
-        for n in op.inputs:
-            out.setdefault(n, []).append(op)
-    return out
-
-
 def fuse(graph: Graph) -> Graph:
-    """Fold `add(matmul, const 1-D bias)` and an optional GELU after it into
-    one `matmul_epilogue` with attr `act` (fuse.py:16-92). The matmul's and
-    the add's intermediates must each have exactly one consumer and not be
-    graph outputs; the fused op keeps the matmul's id."""
-    cons = _consumers(graph)
-    protected = set(graph.outputs)
-
-    def only(name: str, skip: set[int]) -> Op | None:
-        if name in protected:
-            return None
-        found = [o for o in cons.get(name, []) if o.id not in skip]
-        return found[0] if len(found) == 1 and len(cons.get(name, [])) == 1 else None
-
-    consumed: set[int] = set()
-    rewritten: dict[int, Op] = {}
-    dropped: set[str] = set()
-    for op in graph.ops:
-        if op.id in consumed or op.kind != "matmul":
+    """matmul -> add of a 1-D const bias (-> GELU) becomes one
+    `matmul_epilogue(a, w, bias)` with attr `act` ("none" or the GELU's kind),
+    as hexlib/graph/fuse.py:16-92 folds it: the product and the biased sum
+    must each be read by that next op alone and not be graph outputs; the
+    fused op keeps the matmul's id and place and writes the last op's output."""
+    ed = _Edit(graph)
+    for mm in graph.ops:
+        if mm.kind != "matmul" or ed.touched(mm):
             continue
-        mm = op.outputs[0]
-        add = only(mm, consumed)
-        if add is None or add.kind != "add" or len(add.inputs) != 2:
+        product = mm.outputs[0]
+        add = ed.only_reader(product)
+        if add is None or add.kind != "add" or len(add.inputs) != 2 or ed.touched(add):
             continue
-        bias = add.inputs[1] if add.inputs[0] == mm else add.inputs[0]
+        bias = add.inputs[1] if add.inputs[0] == product else add.inputs[0]
         bt = graph.tensors.get(bias)
         if bt is None or not bt.const or len(bt.shape) != 1:
             continue
-        act, tail = "none", add
-        a = only(add.outputs[0], consumed | {add.id})
-        if a is not None and a.kind in FUSABLE_ACTS:
-            act, tail = a.kind, a
-        rewritten[op.id] = Op(op.id, "matmul_epilogue", (op.inputs[0], op.inputs[1], bias),
-                              tail.outputs, {"act": act})
-        consumed.add(add.id)
-        dropped.add(mm)
-        if tail is not add:
-            consumed.add(tail.id)
-            dropped.add(add.outputs[0])
-    if not rewritten:
-        return graph
-    ops = tuple(rewritten.get(o.id, o) for o in graph.ops if o.id not in consumed)
-    tensors = {n: t for n, t in graph.tensors.items() if n not in dropped}
-    return Graph(tensors, ops, graph.inputs, graph.outputs)
+        tail, act = add, "none"
+        gelu = ed.only_reader(add.outputs[0])
+        if gelu is not None and gelu.kind in FUSABLE_ACTS and not ed.touched(gelu):
+            tail, act = gelu, gelu.kind
+        chain = [add] if tail is add else [add, gelu]
+        ed.replace(mm, Op(mm.id, "matmul_epilogue", (mm.inputs[0], mm.inputs[1], bias),
+                          tail.outputs, {"act": act}))
+        ed.remove(chain, [o for c in [mm] + chain[:-1] for o in c.outputs])
+    return ed.result()
 
+
+# ---- CUDA-only rewrites ------------------------------------------------------------------
 
 def fuse_attention(graph: Graph) -> Graph:
     """CUDA-only: scale(q) -> matmul(., transpose_hd(k)) -> softmax -> matmul(., v)
-    becomes one `attention(q, k, v)` op with attr `scale`, and the [H, T, T]
-    scores and probabilities are never written. Each removed intermediate must
-    have exactly one consumer and not be a graph output."""
-    cons = _consumers(graph)
-    protected = set(graph.outputs)
-    producer = {o.outputs[0]: o for o in graph.ops}
-
-    def sole(name):
-        c = cons.get(name, [])
-        return c[0] if len(c) == 1 and name not in protected else None
-
-    consumed: set[int] = set()
-    rewritten: dict[int, Op] = {}
-    dropped: set[str] = set()
+    becomes one `attention(q, k, v)` op with attr `scale` in the place of the
+    last matmul, and the [H, T, T] scores and probabilities are never
+    written. Each removed intermediate must be read by the next op of the
+    chain alone and not be a graph output; q, k, v and the context are fp16
+    [Bn, T, D] of one shape."""
+    ed = _Edit(graph)
+    T = graph.tensors
     for sm in graph.ops:
         if sm.kind != "softmax" or sm.attrs.get("axis") != -1:
             continue
-        qk = producer.get(sm.inputs[0])
-        pv = sole(sm.outputs[0])
-        if qk is None or qk.kind != "matmul" or pv is None or pv.kind != "matmul":
+        qk = ed.written_by(sm.inputs[0], "matmul")
+        pv = ed.only_reader(sm.outputs[0])
+        if qk is None or pv is None or pv.kind != "matmul" or pv.inputs[0] != sm.outputs[0]:
             continue
-        if pv.inputs[0] != sm.outputs[0] or sole(qk.outputs[0]) is not sm:
+        if ed.only_reader(qk.outputs[0]) is not sm:
             continue
-        sc = producer.get(qk.inputs[0])
-        kt = producer.get(qk.inputs[1])
-        if sc is None or sc.kind != "scale" or kt is None or kt.kind != "transpose":
+        sc = ed.written_by(qk.inputs[0], "scale")
+        kt = ed.written_by(qk.inputs[1], "transpose")
+        if sc is None or kt is None or tuple(kt.attrs.get("perm", ())) != (0, 2, 1):
             continue
-        if tuple(kt.attrs.get("perm", ())) != (0, 2, 1):
-            continue
-        if sole(sc.outputs[0]) is not qk or sole(kt.outputs[0]) is not qk:
+        if ed.only_reader(sc.outputs[0]) is not qk or ed.only_reader(kt.outputs[0]) is not qk:
             continue
         q, k, v = sc.inputs[0], kt.inputs[0], pv.inputs[1]
-        shp = graph.tensors[q].shape
-        if len(shp) != 3 or graph.tensors[k].shape != shp or graph.tensors[v].shape != shp:
+        shape = T[q].shape
+        if len(shape) != 3 or T[k].shape != shape or T[v].shape != shape:
             continue
-        if not all(graph.tensors[n].dtype == "fp16" for n in (q, k, v, pv.outputs[0])):
+        if any(T[n].dtype != "fp16" for n in (q, k, v, pv.outputs[0])):
             continue
-        rewritten[pv.id] = Op(pv.id, "attention", (q, k, v), pv.outputs,
-                              {"scale": float(sc.attrs["factor"])})
-        consumed |= {sc.id, kt.id, qk.id, sm.id}
-        dropped |= {sc.outputs[0], kt.outputs[0], qk.outputs[0], sm.outputs[0]}
-    if not rewritten:
-        return graph
-    ops = tuple(rewritten.get(o.id, o) for o in graph.ops if o.id not in consumed)
-    tensors = {n: t for n, t in graph.tensors.items() if n not in dropped}
-    return Graph(tensors, ops, graph.inputs, graph.outputs)
+        ed.replace(pv, pv.with_(kind="attention", inputs=(q, k, v),
+                                attrs={"scale": float(sc.attrs["factor"])}))
+        chain = (sc, kt, qk, sm)
+        ed.remove(chain, [c.outputs[0] for c in chain])
+    return ed.result()
 
 
 def fuse_residual(graph: Graph) -> Graph:
-    """CUDA-only: `add(r, matmul_epilogue(a, w, b))` whose matmul result has
-    no other consumer becomes `matmul_epilogue_residual(a, w, b, r)`; the
-    epilogue rounds the product to fp16 before adding, as the two ops do."""
-    cons = _consumers(graph)
-    protected = set(graph.outputs)
-    producer = {o.outputs[0]: o for o in graph.ops}
-    consumed: set[int] = set()
-    rewritten: dict[int, Op] = {}
-    dropped: set[str] = set()
+    """CUDA-only: `add(r, matmul_epilogue(a, w, b))` whose product nothing
+    else reads becomes `matmul_epilogue_residual(a, w, b, r)` in the add's
+    place (its inputs are all ready there); the epilogue rounds the product to
+    fp16 before adding, as the two ops do. r must be an fp16 activation of
+    the product's shape."""
+    ed = _Edit(graph)
+    T = graph.tensors
     for add in graph.ops:
-        if add.kind != "add" or len(add.inputs) != 2:
+        if add.kind != "add" or len(add.inputs) != 2 or T[add.outputs[0]].dtype != "fp16":
             continue
         for side in (1, 0):
-            mm = producer.get(add.inputs[side])
+            mm = ed.written_by(add.inputs[side], "matmul_epilogue")
             r = add.inputs[1 - side]
-            if mm is None or mm.kind != "matmul_epilogue" or mm.id in consumed:
+            if mm is None or ed.touched(mm) or ed.only_reader(mm.outputs[0]) is not add:
                 continue
-            out = mm.outputs[0]
-            if out in protected or len(cons.get(out, [])) != 1:
+            rt, pt = T[r], T[mm.outputs[0]]
+            if rt.const or rt.dtype != "fp16" or pt.dtype != "fp16" or rt.shape != pt.shape:
                 continue
-            rt, ot = graph.tensors[r], graph.tensors[out]
-            if rt.shape != ot.shape or rt.dtype != "fp16" or ot.dtype != "fp16" or rt.const:
-                continue
-            if graph.tensors[add.outputs[0]].dtype != "fp16":
-                continue
-            rewritten[add.id] = Op(add.id, "matmul_epilogue_residual",
-                                   tuple(mm.inputs) + (r,), add.outputs,
-                                   {"act": mm.attrs.get("act", "none")})
-            consumed.add(mm.id)
-            dropped.add(out)
+            ed.replace(add, add.with_(kind="matmul_epilogue_residual",
+                                      inputs=tuple(mm.inputs) + (r,),
+                                      attrs={"act": mm.attrs.get("act", "none")}))
+            ed.remove([mm], mm.outputs)
             break
-    if not rewritten:
-        return graph
-    # the fused op takes the matmul's place in the order (its inputs are ready there)
-    ops = []
-    for o in graph.ops:
-        if o.id in consumed:
-            continue
-        ops.append(rewritten.get(o.id, o))
-    tensors = {n: t for n, t in graph.tensors.items() if n not in dropped}
-    return Graph(tensors, tuple(ops), graph.inputs, graph.outputs)
+    return ed.result()
 
 
 def fuse_patchify_cast(graph: Graph) -> Graph:
-    """CUDA-only: `cast(patchify(image), fp16)` whose fp32 patch rows have no
-    other consumer becomes one `patchify_cast(image)` writing the fp16 rows
-    (each value rounded to nearest even, as the cast rounds it): one pass
-    over the image instead of a write and a re-read of the fp32 rows."""
-    cons = _consumers(graph)
-    protected = set(graph.outputs)
-    T = graph.tensors
-    rewritten: dict[int, Op] = {}
-    consumed: set[int] = set()
-    dropped: set[str] = set()
+    """CUDA-only: `cast(patchify(image), fp16)` whose fp32 patch rows nothing
+    else reads becomes one `patchify_cast(image)` writing the fp16 rows (each
+    value rounded to nearest even, as the cast rounds it): one pass over the
+    image instead of a write and a re-read of the fp32 rows."""
+    ed = _Edit(graph)
     for pt in graph.ops:
         if pt.kind != "patchify":
             continue
         rows = pt.outputs[0]
-        users = cons.get(rows, [])
-        if rows in protected or len(users) != 1:
+        cast = ed.only_reader(rows)
+        if cast is None or cast.kind != "cast" or cast.attrs.get("dtype") != "fp16":
             continue
-        cast = users[0]
-        if cast.kind != "cast" or cast.attrs.get("dtype") != "fp16" or T[rows].dtype != "fp32":
+        if graph.tensors[rows].dtype != "fp32":
             continue
-        rewritten[pt.id] = Op(pt.id, "patchify_cast", pt.inputs, cast.outputs, dict(pt.attrs))
-        consumed.add(cast.id)
-        dropped.add(rows)
-    if not rewritten:
-        return graph
-    ops = tuple(rewritten.get(o.id, o) for o in graph.ops if o.id not in consumed)
-    tensors = {n: t for n, t in graph.tensors.items() if n not in dropped}
-    return Graph(tensors, ops, graph.inputs, graph.outputs)
+        ed.replace(pt, pt.with_(kind="patchify_cast", outputs=cast.outputs))
+        ed.remove([cast], [rows])
+    return ed.result()
 
 
 def fold_layernorm(graph: Graph, derived_in: Mapping[str, tuple] | None = None
                    ) -> tuple[Graph, dict[str, tuple]]:
     """CUDA-only, after `fuse_qkv`: a `layernorm(x, gamma, beta)` whose only
-    consumer is a GEMM over its output with an fp16 weight W [K, N], N a
+    reader is a GEMM over its output with an fp16 weight W [K, N], N a
     multiple of 256, becomes
 
         stats = ln_stats(x)                                   [T, 2] fp32
@@ -504,29 +607,24 @@ def fold_layernorm(graph: Graph, derived_in: Mapping[str, tuple] | None = None
     so the normalised rows are never written out and read back. The RoPE
     variant takes the two segment tables interleaved ([2T, 2, 16]). New
     consts come back as `{name: (recipe, parts, arg)}` for the batch builder."""
-    cons = _consumers(graph)
-    protected = set(graph.outputs)
+    ed = _Edit(graph)
     T = graph.tensors
-    rewritten: dict[int, Op] = {}
-    new_tensors: dict[str, Tensor] = {}
-    dropped: set[str] = set()
     derived: dict[str, tuple] = {}
     for ln in graph.ops:
         if ln.kind != "layernorm" or len(ln.inputs) != 3:
             continue
         y = ln.outputs[0]
-        users = cons.get(y, [])
-        if y in protected or len(users) != 1:
-            continue
-        mm = users[0]
-        if mm.kind not in ("matmul_epilogue", "matmul_epilogue_rope") or mm.inputs[0] != y:
+        mm = ed.only_reader(y)
+        if mm is None or mm.kind not in ("matmul_epilogue", "matmul_epilogue_rope") \
+                or mm.inputs[0] != y:
             continue
         x, gamma, beta = ln.inputs
         w, b = mm.inputs[1], mm.inputs[2]
         wt, bt, xt = T[w], T[b], T[x]
-        if not (wt.const and wt.dtype == "fp16" and len(wt.shape) == 2 and bt.const and
-                bt.dtype == "fp32" and T[gamma].const and T[beta].const and
-                T[gamma].dtype == "fp32" and T[beta].dtype == "fp32"):
+        consts_ok = (wt.const and wt.dtype == "fp16" and len(wt.shape) == 2 and bt.const
+                     and bt.dtype == "fp32" and all(T[n].const and T[n].dtype == "fp32"
+                                                    for n in (gamma, beta)))
+        if not consts_ok:
             continue
         K, N = wt.shape
         if N % 256 or len(xt.shape) != 2 or xt.shape[1] != K or xt.dtype != "fp16":
@@ -537,38 +635,30 @@ def fold_layernorm(graph: Graph, derived_in: Mapping[str, tuple] | None = None
             if rec is None or rec[0] != "rope_segments":
                 continue
             rope_src = tuple(rec[1])
-        n_tok = xt.shape[0]
-        wf = f"lnfold_w({gamma},{w})"
-        cols = f"lnfold_cols({gamma},{beta},{w},{b})"
-        stats = f"{y}+stats"
-        new_tensors[wf] = Tensor(wf, "fp16", (K, N), True)
-        new_tensors[cols] = Tensor(cols, "fp32", (2, N), True)
-        new_tensors[stats] = Tensor(stats, "fp32", (n_tok, 2), False)
+        wf = ed.add_tensor(Tensor(f"lnfold_w({gamma},{w})", "fp16", (K, N), True))
+        cols = ed.add_tensor(Tensor(f"lnfold_cols({gamma},{beta},{w},{b})", "fp32", (2, N),
+                                    True))
+        stats = ed.add_tensor(Tensor(f"{y}+stats", "fp32", (xt.shape[0], 2)))
         derived[wf] = ("ln_fold_w", (gamma, w), 0)
         derived[cols] = ("ln_fold_cols", (gamma, beta, w, b), 0)
-        rewritten[ln.id] = Op(ln.id, "ln_stats", (x,), (stats,), {"eps": float(ln.attrs["eps"])})
+        ed.replace(ln, ln.with_(kind="ln_stats", inputs=(x,), outputs=(stats,),
+                                attrs={"eps": float(ln.attrs["eps"])}))
         act = {"act": mm.attrs.get("act", "none")}
-        if mm.kind == "matmul_epilogue":
-            rewritten[mm.id] = Op(mm.id, "matmul_epilogue_ln", (x, wf, cols, stats),
-                                  mm.outputs, act)
+        if rope_src is None:
+            ed.replace(mm, mm.with_(kind="matmul_epilogue_ln", inputs=(x, wf, cols, stats),
+                                    attrs=act))
         else:
-            seg_cos, seg_idx = mm.inputs[3], mm.inputs[5]
             cos, sin = rope_src
-            segtab = f"rope_segtab({cos},{sin})"
-            new_tensors[segtab] = Tensor(segtab, "fp32", (T[seg_cos].shape[0], 2, 16), True)
+            segtab = ed.add_tensor(Tensor(f"rope_segtab({cos},{sin})", "fp32",
+                                          (T[mm.inputs[3]].shape[0], 2, 16), True))
             derived[segtab] = ("rope_segtab", (cos, sin), 0)
-            rewritten[mm.id] = Op(mm.id, "matmul_epilogue_ln_rope",
-                                  (x, wf, cols, stats, segtab, seg_idx), mm.outputs,
-                                  dict(act, rope_cols=int(mm.attrs["rope_cols"])))
-        dropped.add(y)
-    if not rewritten:
+            ed.replace(mm, mm.with_(kind="matmul_epilogue_ln_rope",
+                                    inputs=(x, wf, cols, stats, segtab, mm.inputs[5]),
+                                    attrs=dict(act, rope_cols=int(mm.attrs["rope_cols"]))))
+        ed.remove([], [y])
+    if not derived:
         return graph, {}
-    ops = tuple(rewritten.get(o.id, o) for o in graph.ops)
-    tensors = {n: t for n, t in graph.tensors.items() if n not in dropped}
-    tensors.update(new_tensors)
-    used = {n for o in ops for n in o.inputs}
-    tensors = {n: t for n, t in tensors.items() if not (t.const and n not in used)}
-    return Graph(tensors, ops, graph.inputs, graph.outputs), derived
+    return ed.result(prune_consts=True), derived
 
 
 def fuse_qkv(graph: Graph, rope_epilogue: bool = False) -> tuple[Graph, dict[str, tuple]]:
@@ -594,62 +684,51 @@ def fuse_qkv(graph: Graph, rope_epilogue: bool = False) -> tuple[Graph, dict[str
     grid, so the distinct ones are few and stay cache-resident under the
     epilogue); the batch builder refuses tables that are not half-symmetric.
 
-    The concatenated weight and bias and the segment tables are new consts,
+    The packed GEMM takes the q projection's place, rope_qk the k
+    projection's (id and place), attention_qkv the final transpose's. The
+    concatenated weight and bias and the segment tables are new consts,
     returned as `{name: ("concat", (parts...), axis)}` and
     `{name: ("rope_segments", (cos, sin), which)}` for the batch builder to
-    derive from the feeds. Every removed intermediate must have exactly one
-    consumer and not be a graph output; anything else leaves the block as it
-    was."""
-    cons = _consumers(graph)
-    protected = set(graph.outputs)
-    producer = {o.outputs[0]: o for o in graph.ops}
+    derive from the feeds. Every removed intermediate must be read by its
+    chain's next op alone and not be a graph output; anything else leaves the
+    block as it was."""
+    ed = _Edit(graph)
     T = graph.tensors
-
-    def sole_user(name):
-        c = cons.get(name, [])
-        return c[0] if len(c) == 1 and name not in protected else None
-
-    def prod(name, kind):
-        o = producer.get(name)
-        return o if o is not None and o.kind == kind and sole_user(name) is not None else None
-
-    consumed: set[int] = set()
-    rewritten: dict[int, Op] = {}
-    new_tensors: dict[str, Tensor] = {}
-    dropped: set[str] = set()
     derived: dict[str, tuple] = {}
+
+    def step_back(name: str, kind: str) -> Op | None:
+        """The op of `kind` that writes `name`, if `name` has one reader."""
+        op = ed.written_by(name, kind)
+        return op if op is not None and ed.only_reader(name) is not None else None
+
+    def projection(name: str, roped: bool):
+        """transpose <- [rope_2d <-] reshape <- matmul_epilogue (no act)."""
+        tr = step_back(name, "transpose")
+        if tr is None or tuple(tr.attrs.get("perm", ())) != (1, 0, 2):
+            return None
+        rp = step_back(tr.inputs[0], "rope_2d") if roped else None
+        if roped and rp is None:
+            return None
+        rs = step_back((rp or tr).inputs[0], "reshape")
+        mm = step_back(rs.inputs[0], "matmul_epilogue") if rs is not None else None
+        if mm is None or mm.attrs.get("act", "none") != "none":
+            return None
+        return [o for o in (tr, rp, rs, mm) if o is not None], mm, rp
+
     for att in graph.ops:
         if att.kind != "attention":
             continue
-        chain = {}
-        ok = True
-        for which, name, roped in (("q", att.inputs[0], True), ("k", att.inputs[1], True),
-                                   ("v", att.inputs[2], False)):
-            tr = prod(name, "transpose")
-            if tr is None or tuple(tr.attrs.get("perm", ())) != (1, 0, 2):
-                ok = False
-                break
-            rp = prod(tr.inputs[0], "rope_2d") if roped else None
-            if roped and rp is None:
-                ok = False
-                break
-            rs = prod((rp.inputs[0] if roped else tr.inputs[0]), "reshape")
-            mm = prod(rs.inputs[0], "matmul_epilogue") if rs is not None else None
-            if mm is None or mm.attrs.get("act", "none") != "none":
-                ok = False
-                break
-            chain[which] = (tr, rp, rs, mm)
-        if not ok:
+        found = [projection(n, roped) for n, roped in zip(att.inputs, (True, True, False))]
+        if any(f is None for f in found):
             continue
-        ctx_t = sole_user(att.outputs[0])
-        if ctx_t is None or ctx_t.kind != "transpose" or tuple(ctx_t.attrs.get("perm", ())) != (1, 0, 2):
+        back = ed.only_reader(att.outputs[0])
+        if back is None or back.kind != "transpose" or \
+                tuple(back.attrs.get("perm", ())) != (1, 0, 2):
             continue
-        mms = [chain[w][3] for w in "qkv"]
+        mms = [f[1] for f in found]
         a = mms[0].inputs[0]
-        if any(m.inputs[0] != a for m in mms):
-            continue
-        rq, rk = chain["q"][1], chain["k"][1]
-        if rq.inputs[1:] != rk.inputs[1:]:
+        rq, rk = found[0][2], found[1][2]
+        if any(m.inputs[0] != a for m in mms) or rq.inputs[1:] != rk.inputs[1:]:
             continue
         cos, sin = rq.inputs[1], rq.inputs[2]
         ws = [m.inputs[1] for m in mms]
@@ -660,59 +739,42 @@ def fuse_qkv(graph: Graph, rope_epilogue: bool = False) -> tuple[Graph, dict[str
             continue
         if not all(T[b].const and T[b].dtype == "fp32" for b in bs):
             continue
-        n_tok, heads, d = T[att.outputs[0]].shape[1], T[att.outputs[0]].shape[0], T[att.outputs[0]].shape[2]
+        heads, n_tok, d = T[att.outputs[0]].shape
         K = T[ws[0]].shape[0]
         if any(T[w].shape != (K, heads * d) for w in ws) or T[a].shape != (n_tok, K) or d != 64:
             continue
-        wname = f"concat({ws[0]},{ws[1]},{ws[2]})"
-        bname = f"concat({bs[0]},{bs[1]},{bs[2]})"
-        raw = f"{mms[0].outputs[0]}+qkv.raw"
-        qkv = f"{mms[0].outputs[0]}+qkv"
-        new_tensors[wname] = Tensor(wname, wdt, (K, 3 * heads * d), True)
-        new_tensors[bname] = Tensor(bname, "fp32", (3 * heads * d,), True)
-        new_tensors[raw] = Tensor(raw, "fp16", (n_tok, 3, heads, d), False)
-        new_tensors[qkv] = Tensor(qkv, "fp16", (n_tok, 3, heads, d), False)
+        width = 3 * heads * d
+        wname = ed.add_tensor(Tensor(f"concat({ws[0]},{ws[1]},{ws[2]})", wdt, (K, width), True))
+        bname = ed.add_tensor(Tensor(f"concat({bs[0]},{bs[1]},{bs[2]})", "fp32", (width,), True))
         derived[wname] = ("concat", tuple(ws), 1)
         derived[bname] = ("concat", tuple(bs), 0)
+        qkv = ed.add_tensor(Tensor(f"{mms[0].outputs[0]}+qkv", "fp16", (n_tok, 3, heads, d)))
+        for f in found:
+            ed.remove(f[0], [o.outputs[0] for o in f[0]])
+        ed.remove([att], att.outputs)
         if rope_epilogue and wdt == "fp16":
-            segs = tuple(f"rope_segments({cos},{sin}).{w}" for w in ("cos", "sin", "idx"))
-            new_tensors[segs[0]] = Tensor(segs[0], "fp32", (2 * n_tok, 16), True)
-            new_tensors[segs[1]] = Tensor(segs[1], "fp32", (2 * n_tok, 16), True)
-            new_tensors[segs[2]] = Tensor(segs[2], "int32", (n_tok, 2), True)
-            for i, sname in enumerate(segs):
+            segs = []
+            for i, (part, dt, shape) in enumerate((("cos", "fp32", (2 * n_tok, 16)),
+                                                   ("sin", "fp32", (2 * n_tok, 16)),
+                                                   ("idx", "int32", (n_tok, 2)))):
+                sname = ed.add_tensor(Tensor(f"rope_segments({cos},{sin}).{part}", dt, shape,
+                                             True))
                 derived[sname] = ("rope_segments", (cos, sin), i)
-            del new_tensors[raw]
-            rewritten[mms[0].id] = Op(mms[0].id, "matmul_epilogue_rope",
-                                      (a, wname, bname) + segs, (qkv,),
-                                      {"act": "none", "rope_cols": 2 * heads * d})
+                segs.append(sname)
+            ed.replace(mms[0], Op(mms[0].id, "matmul_epilogue_rope",
+                                  (a, wname, bname, *segs), (qkv,),
+                                  {"act": "none", "rope_cols": 2 * heads * d}))
         else:
-            rewritten[mms[0].id] = Op(mms[0].id, "matmul_epilogue", (a, wname, bname), (raw,),
-                                      {"act": "none"})
-            # the rope takes the k projection's op id, free once that op is gone
-            rewritten[mms[1].id] = Op(mms[1].id, "rope_qk", (raw, cos, sin), (qkv,), {})
-        rewritten[ctx_t.id] = Op(ctx_t.id, "attention_qkv", (qkv,), ctx_t.outputs,
-                                 {"scale": float(att.attrs["scale"])})
-        for w in "qkv":
-            tr, rp, rs, mm = chain[w]
-            for o in (tr, rp, rs, mm):
-                if o is not None:
-                    consumed.add(o.id)
-                    dropped.add(o.outputs[0])
-        consumed.add(att.id)
-        dropped.add(att.outputs[0])
-        consumed.discard(mms[0].id)
-        if mms[1].id in rewritten:
-            consumed.discard(mms[1].id)
-    if not rewritten:
+            raw = ed.add_tensor(Tensor(f"{mms[0].outputs[0]}+qkv.raw", "fp16",
+                                       (n_tok, 3, heads, d)))
+            ed.replace(mms[0], Op(mms[0].id, "matmul_epilogue", (a, wname, bname), (raw,),
+                                  {"act": "none"}))
+            ed.replace(mms[1], Op(mms[1].id, "rope_qk", (raw, cos, sin), (qkv,), {}))
+        ed.replace(back, back.with_(kind="attention_qkv", inputs=(qkv,),
+                                    attrs={"scale": float(att.attrs["scale"])}))
+    if not derived:
         return graph, {}
-    ops = tuple(rewritten.get(o.id, o) for o in graph.ops
-                if o.id not in consumed or o.id in rewritten)
-    tensors = {n: t for n, t in graph.tensors.items() if n not in dropped}
-    tensors.update(new_tensors)
-    used = {n for o in ops for n in o.inputs}
-    tensors = {n: t for n, t in tensors.items()
-               if not (t.const and n not in used)}
-    return Graph(tensors, ops, graph.inputs, graph.outputs), derived
+    return ed.result(prune_consts=True), derived
 
 
 # ---- the executable plan -------------------------------------------------------------
