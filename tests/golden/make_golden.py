@@ -33,7 +33,10 @@ repository's code in the loop:
                 replaced by its dequantized value rounded to fp16 (the
                 arithmetic the DSP kernel performs, baseline.c:36-47).
 
-`--quant-only` regenerates quant.npz alone.
+  tiny_params.npz  the tiny golden's upstream parameters as stored (the input
+                the reference's loader.feeds_from_params maps to tiny.npz's feeds).
+
+`--quant-only` regenerates quant.npz alone, `--params-only` tiny_params.npz alone.
 
 The fixtures are small (the biggest is well under 2 MB) and are committed;
 tests read them without the reference present.
@@ -270,12 +273,27 @@ def make_quant(ref_root: str) -> None:
     print("wrote quant.npz")
 
 
+def make_params(ref_root: str) -> None:
+    """tiny_params.npz: the upstream (transformers-named) parameters of the
+    reference's tiny golden, exactly as stored there -- the input of
+    hexlib/models/loader.py feeds_from_params, whose output is tiny.npz's
+    feed::* arrays."""
+    z = np.load(os.path.join(ref_root, "hexlib", "tests", "data", "qwen35_vision_tiny.npz"))
+    params = {k: z[k] for k in z.files if k.startswith("param::")}
+    np.savez_compressed(os.path.join(HERE, "tiny_params.npz"), **params)
+    print(f"wrote tiny_params.npz ({len(params)} parameters)")
+
+
 if __name__ == "__main__":
     args = [a for a in sys.argv[1:] if not a.startswith("--")]
     root = args[0] if args else os.environ.get("HEXLIB_REFERENCE")
     if not root:
         sys.exit("usage: python tests/golden/make_golden.py /path/to/hexlib-checkout "
-                 "[--quant-only] (or set HEXLIB_REFERENCE)")
+                 "[--quant-only | --params-only] (or set HEXLIB_REFERENCE)")
+    if "--params-only" in sys.argv:
+        make_params(root)
+        sys.exit(0)
     if "--quant-only" not in sys.argv:
         main(root)
+        make_params(root)
     make_quant(root)
