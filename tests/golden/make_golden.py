@@ -36,7 +36,11 @@ repository's code in the loop:
   tiny_params.npz  the tiny golden's upstream parameters as stored (the input
                 the reference's loader.feeds_from_params maps to tiny.npz's feeds).
 
-`--quant-only` regenerates quant.npz alone, `--params-only` tiny_params.npz alone.
+  qwen35_256_compiled.json.gz  compiled.to_json of the reference's own 256^2
+                fp16-weight plan (gzip).
+
+`--quant-only` regenerates quant.npz alone, `--params-only` tiny_params.npz
+alone, `--compiled-only` qwen35_256_compiled.json.gz alone.
 
 The fixtures are small (the biggest is well under 2 MB) and are committed;
 tests read them without the reference present.
@@ -273,6 +277,26 @@ def make_quant(ref_root: str) -> None:
     print("wrote quant.npz")
 
 
+def make_compiled(ref_root: str) -> None:
+    """qwen35_256_compiled.json.gz: hexlib.graph.compiled.to_json of the
+    reference's own compile_model plan for the 256^2 encoder with fp16
+    weights (VTCM budget 8 MiB), gzip-compressed."""
+    import gzip
+    sys.path.insert(0, ref_root)
+    import hexlib.graph.opdefs  # noqa: F401 -- registers the op kinds
+    from hexlib.graph import compiled
+    from hexlib.graph.pipeline import compile_model
+    from hexlib.models.qwen35 import qwen35_at
+    from hexlib.models.vit import build_vision_encoder
+    from hexlib.result import Err
+    cfg = dataclasses.replace(qwen35_at(256), weight_dtype="fp16")
+    m = compile_model(build_vision_encoder(cfg), budget=8 << 20)
+    assert not isinstance(m, Err), m
+    with gzip.open(os.path.join(HERE, "qwen35_256_compiled.json.gz"), "wt") as fh:
+        fh.write(compiled.to_json(m))
+    print("wrote qwen35_256_compiled.json.gz")
+
+
 def make_params(ref_root: str) -> None:
     """tiny_params.npz: the upstream (transformers-named) parameters of the
     reference's tiny golden, exactly as stored there -- the input of
@@ -289,11 +313,15 @@ if __name__ == "__main__":
     root = args[0] if args else os.environ.get("HEXLIB_REFERENCE")
     if not root:
         sys.exit("usage: python tests/golden/make_golden.py /path/to/hexlib-checkout "
-                 "[--quant-only | --params-only] (or set HEXLIB_REFERENCE)")
+                 "[--quant-only | --params-only | --compiled-only] (or set HEXLIB_REFERENCE)")
     if "--params-only" in sys.argv:
         make_params(root)
+        sys.exit(0)
+    if "--compiled-only" in sys.argv:
+        make_compiled(root)
         sys.exit(0)
     if "--quant-only" not in sys.argv:
         main(root)
         make_params(root)
+        make_compiled(root)
     make_quant(root)

@@ -57,6 +57,24 @@ def test_reference_plan_json_loads_in_plan_order():
     assert [s.op.id for s in ep.plan.steps] == PLANS["tiny_fp16"]["step_order"]
 
 
+def test_the_references_256_json_plan_is_our_256_plan():
+    """The reference's compiled.to_json artefact of its 256^2 plan loads into
+    the same graph this module builds, in the reference's step order."""
+    import gzip
+    with gzip.open(os.path.join(GOLDEN, "qwen35_256_compiled.json.gz"), "rt") as fh:
+        ep = G.from_compiled_json(fh.read())
+    ours = G.compile_for_cuda(G.build_vision_encoder(G.qwen35_at(256))).graph
+    assert [o.id for o in ep.graph.ops] == PLANS["qwen35_256"]["step_order"]
+    assert {n: (t.dtype, t.shape, t.const) for n, t in ep.graph.tensors.items()} == \
+        {n: (t.dtype, t.shape, t.const) for n, t in ours.tensors.items()}
+    by_id = {o.id: o for o in ours.ops}
+    for o in ep.graph.ops:
+        mine = by_id[o.id]
+        assert (o.kind, o.inputs, o.outputs) == (mine.kind, mine.inputs, mine.outputs)
+        assert _norm_attrs(o.attrs) == _norm_attrs(mine.attrs)
+    assert ep.graph.problems() == []
+
+
 def test_encoder_op_census_at_256():
     ep = G.compile_for_cuda(G.build_vision_encoder(G.qwen35_at(256)))
     c = Counter(o.kind for o in ep.graph.ops)
