@@ -15,6 +15,9 @@ collective. One step = the whole encoder over the whole batch.
            from pinned memory, the plan, the device->host copy of the
            embeddings (and the all-gather for N > 1); one step's copies
            overlap the other session's kernels.
+  gather   N > 1: the embedding all-gather runs through the library's NCCL
+           entry points (hexlib_b200_nccl_*, a deadline on every wait); its
+           own device time per step is reported as gather_ms_per_step.
   roofline the dominant kernel (largest share of eager, op-by-op timed
            passes; each op's median of three): algorithmic FLOPs or bytes per
            launch / its mean CUDA-event duration, against MEASURED_PEAKS.json.
@@ -345,19 +348,30 @@ def run_b200(args) -> None:
     emb = s.device_view(plan.outputs[0], n)
 
     gather_events: list = []
+    # The embedding all-gather (N > 1) through the library's NCCL entry points,
+    # every wait bounded; one gathered [B, T/4, C_out] buffer per session.
+    gatherer = D.EmbeddingGather(rank, world, local, timeout_s=120.0) if pg is not None else None
+    gathered: dict = {}
+
+    def gather_on(sess, view):
+        buf = gathered.get(id(sess))
+        if buf is None:
+            buf = torch.empty((world * n,) + tuple(view.shape[1:]), dtype=torch.float16,
+                              device=view.device)
+            gathered[id(sess)] = buf
+        gatherer.gather(view, buf, sess.stream())
 
     def step_device(timed=False):
         s.invoke(n, sync=False)
-        if pg is not None:
-            with torch.cuda.stream(stream):
-                if timed:   # the all-gather's own device time, on the session stream
-                    g0 = torch.cuda.Event(enable_timing=True)
-                    g1 = torch.cuda.Event(enable_timing=True)
-                    g0.record(stream)
-                D.gather_embeddings(emb)
-                if timed:
-                    g1.record(stream)
-                    gather_events.append((g0, g1))
+        if gatherer is not None:
+            if timed:   # the all-gather's own device time, on the session stream
+                g0 = torch.cuda.Event(enable_timing=True)
+                g1 = torch.cuda.Event(enable_timing=True)
+                g0.record(stream)
+            gather_on(s, emb)
+            if timed:
+                g1.record(stream)
+                gather_events.append((g0, g1))
 
     def barrier():
         if pg is not None:
@@ -413,9 +427,8 @@ def run_b200(args) -> None:
     def step_e2e(k):
         j = k % len(pipe.sessions)
         pipe.submit(host_in, host_outs[j])
-        if pg is not None:
-            with torch.cuda.stream(streams[j]):
-                D.gather_embeddings(views[j])
+        if gatherer is not None:
+            gather_on(pipe.sessions[j], views[j])
 
     for k in range(len(pipe.sessions)):      # the new session captures its graph
         step_e2e(k)
@@ -537,10 +550,14 @@ def run_b200(args) -> None:
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
+    if gatherer is not None:
+        for sess in pipe.sessions:
+            gatherer.wait(sess.stream())
     pipe.close()
     s.close()
     if pg is not None:
         pg.barrier()
+        gatherer.close()
         pg.destroy_process_group()
 
 

@@ -46,6 +46,13 @@ _PROTOS: dict[str, list] = {
     "hexlib_b200_diag_wait_timeout": [c_vp, c_u32],
     "hexlib_b200_diag_wait_timeout_stream": [c_u32, c_vp],
     "hexlib_b200_stream_status": [c_vp],
+    "hexlib_b200_nccl_available": [],
+    "hexlib_b200_nccl_unique_id": [c_vp],
+    "hexlib_b200_nccl_open": [c_vp, c_int, c_int, c_int, c_u32, ctypes.POINTER(c_vp)],
+    "hexlib_b200_nccl_allgather_f16": [c_vp, c_vp, c_vp, c_u64, c_vp, c_u32],
+    "hexlib_b200_nccl_wait": [c_vp, c_vp, c_u32],
+    "hexlib_b200_nccl_abort": [c_vp],
+    "hexlib_b200_nccl_close": [c_vp, c_u32],
     "hexlib_b200_check_batch": [c_vp, c_u32, ctypes.POINTER(c_u64), c_u32,
                                 c_u32, c_vp, c_u32, ctypes.POINTER(c_u32)],
     "hexlib_b200_add_fp16": [c_vp, c_vp, c_vp, c_int, c_vp],

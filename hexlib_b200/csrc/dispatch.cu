@@ -973,6 +973,7 @@ const char* hexlib_b200_status_name(int s) {
     case HEXLIB_B200_ERR_CACHE: return "ERR_CACHE";
     case HEXLIB_B200_ERR_CUDA: return "ERR_CUDA";
     case HEXLIB_B200_ERR_TIMEOUT: return "ERR_TIMEOUT";
+    case HEXLIB_B200_ERR_COMM: return "ERR_COMM";
     default: return "UNKNOWN";
   }
 }

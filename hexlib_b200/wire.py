@@ -6,7 +6,8 @@ dispatcher consumes in place of the DSP's -- so the constants, the struct
 layouts and the host-side refusals are the reference's. Two things are added,
 both invisible to a blob the reference would build:
 
-  * status codes 16 (ERR_CUDA) and 17 (ERR_TIMEOUT), appended after 15;
+  * status codes 16 (ERR_CUDA), 17 (ERR_TIMEOUT) and 18 (ERR_COMM), appended
+    after 15;
   * BUF_PER_IMAGE, a bit in `BufDesc.flags` (which the reference always
     writes 0) marking a buffer whose tensors exist once per image, so one
     blob serves a batch of B images.
@@ -34,7 +35,7 @@ STATUS = {
     "ERR_VTCM_TOO_SMALL": 11, "ERR_VTCM_RECLAIMED": 12, "ERR_REQUIRES": 13,
     "ERR_NOT_STARTED": 14, "ERR_CACHE": 15,
     # appended by this backend
-    "ERR_CUDA": 16, "ERR_TIMEOUT": 17,
+    "ERR_CUDA": 16, "ERR_TIMEOUT": 17, "ERR_COMM": 18,
 }
 STATUS_NAME = {v: k for k, v in STATUS.items()}
 

@@ -23,7 +23,7 @@
  *
  * STATUS CODES are hexlib_dsp.h's (:31-54) number for number: OK is 1, so a
  * zero-filled response can never read as success. Codes this backend needs and
- * the DSP did not are APPENDED (16, 17), never renumbered.
+ * the DSP did not are APPENDED (16, 17, 18), never renumbered.
  *
  * THREADING. A session is single-threaded and `invoke` is not reentrant, the
  * same contract as hexlib_dispatch_batch (skel_dispatch.c:134-147). Use one
@@ -58,6 +58,7 @@ extern "C" {
 /* Appended for this backend. */
 #define HEXLIB_B200_ERR_CUDA           16  /* a CUDA runtime call failed        */
 #define HEXLIB_B200_ERR_TIMEOUT        17  /* a device-side bounded wait expired */
+#define HEXLIB_B200_ERR_COMM           18  /* a collective failed or a peer left  */
 
 /* ---- wire constants: hexlib/runtime/wire.py:24-31, hexlib_dsp.h:23-30 ---- */
 #define HEXLIB_B200_BATCH_MAGIC   0x424C5848u  /* 'HXLB' */
@@ -372,6 +373,42 @@ HEXLIB_B200_API int hexlib_b200_attention_qkv_fp16(const void *qkv, void *ctx,
 HEXLIB_B200_API int hexlib_b200_attention_fp16(const void *q, const void *k, const void *v,
                                void *ctx, int Bn, int T, int D, float scale,
                                void *stream);
+
+/* ---- the embedding gather across GPUs (NCCL, with deadlines) --------------
+ * The image-sharded encoder's one exchange: an all-gather of every rank's fp16
+ * embeddings. No counterpart in the reference, which runs one image at a time
+ * on one DSP (skel_dispatch.c:248); the session lifecycle mirrors
+ * hexlib_iface.idl:28-67 (open -> work -> close) and, like every entry here,
+ * fails by default rather than hang: every wait has a deadline, after which
+ * the communicator is aborted and the call answers ERR_TIMEOUT (a peer that
+ * stopped answering) or ERR_COMM (NCCL reported an error, e.g. a peer that
+ * left). An aborted communicator answers ERR_COMM to any further work;
+ * close it and open a new one. NCCL is loaded at run time. */
+#define HEXLIB_B200_NCCL_ID_BYTES 128
+typedef struct hexlib_b200_comm hexlib_b200_comm;
+
+/* 1 when NCCL could be loaded, else 0. */
+HEXLIB_B200_API int hexlib_b200_nccl_available(void);
+/* Rank 0's rendezvous id (128 bytes), to be shared with every rank. */
+HEXLIB_B200_API int hexlib_b200_nccl_unique_id(uint8_t *id_out);
+/* Join the communicator `id` as `rank` of `nranks` on CUDA device `device`,
+ * non-blocking, waiting at most timeout_ms for every rank to join. */
+HEXLIB_B200_API int hexlib_b200_nccl_open(const uint8_t *id, int nranks, int rank,
+                                          int device, uint32_t timeout_ms,
+                                          hexlib_b200_comm **out);
+/* Enqueue on `stream` the all-gather of `count` fp16 values from every rank:
+ * recv holds nranks * count values in rank order. Returns once NCCL has
+ * enqueued it (at most timeout_ms); completion is hexlib_b200_nccl_wait's. */
+HEXLIB_B200_API int hexlib_b200_nccl_allgather_f16(hexlib_b200_comm *comm, const void *send,
+                                                   void *recv, uint64_t count, void *stream,
+                                                   uint32_t timeout_ms);
+/* Wait at most timeout_ms for `stream` (and the gathers on it) to drain. */
+HEXLIB_B200_API int hexlib_b200_nccl_wait(hexlib_b200_comm *comm, void *stream,
+                                          uint32_t timeout_ms);
+/* Abort the communicator now (its kernels return; later calls answer ERR_COMM). */
+HEXLIB_B200_API int hexlib_b200_nccl_abort(hexlib_b200_comm *comm);
+/* Finalize (at most timeout_ms; 0 means 10 s) and free the communicator. */
+HEXLIB_B200_API int hexlib_b200_nccl_close(hexlib_b200_comm *comm, uint32_t timeout_ms);
 
 #ifdef __cplusplus
 }

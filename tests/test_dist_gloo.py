@@ -81,3 +81,74 @@ def test_a_rank_that_leaves_is_an_error_for_the_other(tmp_path):
     assert procs[1].exitcode == 3
     assert not (tmp_path / "rank0.npy").exists()
     assert (tmp_path / "rank0.err").exists()
+
+
+def _id_worker(rank, world, port, out_dir, leave_rank):
+    import datetime
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port),
+                      RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=20))
+    if rank == leave_rank:
+        raise SystemExit(3)       # leaves before the rendezvous id is shared
+    try:
+        ident = D.share_unique_id(rank)
+        with open(os.path.join(out_dir, f"id{rank}.bin"), "wb") as f:
+            f.write(ident)
+    except Exception as e:  # noqa: BLE001 -- recorded for the parent
+        with open(os.path.join(out_dir, f"id{rank}.err"), "w") as f:
+            f.write(type(e).__name__)
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:  # noqa: BLE001
+            pass
+
+
+def test_every_rank_receives_rank0s_nccl_rendezvous_id(tmp_path):
+    """The id is made by the library (no GPU needed) on rank 0 only and
+    reaches every rank byte for byte through the process group."""
+    from hexlib_b200 import _lib
+    if not _lib.lib().hexlib_b200_nccl_available():
+        pytest.skip("NCCL cannot be loaded in this process")
+    port = _free_port()
+    mp.start_processes(_id_worker, args=(3, port, str(tmp_path), -1), nprocs=3,
+                       start_method="spawn", join=True)
+    ids = [(tmp_path / f"id{r}.bin").read_bytes() for r in range(3)]
+    assert len(ids[0]) == 128 and ids[0] == ids[1] == ids[2] and any(ids[0])
+
+
+def test_a_rank_that_leaves_before_the_rendezvous_is_an_error_for_the_others(tmp_path):
+    import multiprocessing
+    port = _free_port()
+    ctx = multiprocessing.get_context("spawn")
+    procs = [ctx.Process(target=_id_worker, args=(r, 2, port, str(tmp_path), 1))
+             for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=90)
+    for p in procs:
+        if p.is_alive():          # never expected: the group timeout is 20 s
+            p.kill()
+            p.join()
+    assert procs[1].exitcode == 3
+    assert not (tmp_path / "id0.bin").exists()
+    assert (tmp_path / "id0.err").exists()
+
+
+def test_the_nccl_entries_refuse_bad_arguments_without_a_device():
+    import ctypes
+
+    from hexlib_b200 import _lib, wire
+    L = _lib.lib()
+    h = ctypes.c_void_p()
+    ident = (ctypes.c_uint8 * 128)()
+    for nranks, rank, timeout in ((0, 0, 100), (2, 2, 100), (2, -1, 100), (2, 0, 0)):
+        assert L.hexlib_b200_nccl_open(ident, nranks, rank, 0, timeout, ctypes.byref(h)) == \
+            wire.STATUS["ERR_INVAL_PARAMS"]
+        assert h.value is None
+    assert L.hexlib_b200_nccl_allgather_f16(None, None, None, 8, None, 100) == \
+        wire.STATUS["ERR_NOT_STARTED"]
+    assert L.hexlib_b200_nccl_wait(None, None, 100) == wire.STATUS["ERR_NOT_STARTED"]
+    assert L.hexlib_b200_nccl_unique_id(None) == wire.STATUS["ERR_INVAL_PARAMS"]
+    assert L.hexlib_b200_nccl_close(None, 0) == wire.STATUS["OK"]
