@@ -493,7 +493,7 @@ def run_b200(args) -> None:
 
     # ---- parity: this step's first image against the oracle (untimed) ----------------
     s.invoke(n)                                  # one more graph replay
-    got0 = s.read_output(plan.outputs[0], 1)[0]
+    got0 = s.read_output(plan.outputs[0], n)[0]   # per-image tensors sit at offset x n
     cpu, parity = None, None
     if rank == 0:
         if world == 1 and os.environ.get("HEXLIB_B200_BENCH_NO_CPU") != "1":

@@ -65,11 +65,13 @@ def _stale(target: str, deps: list[str]) -> bool:
     return any(os.path.getmtime(d) > t for d in deps)
 
 
-def _compile(nvcc: str, src: str, verbose: bool) -> str:
-    obj = os.path.join(BUILD_DIR, os.path.basename(src)[:-3] + ".o")
+def _compile(nvcc: str, src: str, verbose: bool, build_dir: str = BUILD_DIR,
+             defines: tuple[str, ...] = ()) -> str:
+    obj = os.path.join(build_dir, os.path.basename(src)[:-3] + ".o")
     if not _stale(obj, [src] + _headers()):
         return obj
-    cmd = [nvcc, *ARCH_FLAGS, *NVCC_FLAGS, "-I", INCLUDE, "-c", src, "-o", obj]
+    cmd = [nvcc, *ARCH_FLAGS, *NVCC_FLAGS, *(f"-D{d}" for d in defines), "-I", INCLUDE,
+           "-c", src, "-o", obj]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     r = subprocess.run(cmd, capture_output=True, text=True)
@@ -80,22 +82,32 @@ def _compile(nvcc: str, src: str, verbose: bool) -> str:
     return obj
 
 
-def build(verbose: bool = False) -> str:
-    """Compile every kernel and the C ABI; return the path of the library."""
+def build(verbose: bool = False, measure: bool = False) -> str:
+    """Compile every kernel and the C ABI; return the path of the library.
+
+    `measure` builds the measurement variant instead, into
+    _lib/libhexlib_b200_measure.so: the same code with
+    HEXLIB_B200_MEASUREMENT_KNOBS defined, so that a few environment
+    variables (HEXLIB_B200_GEMM_TILE, HEXLIB_B200_GEMM_PAIR[_RES],
+    HEXLIB_B200_WALK_ORDER) can pin a kernel variant for
+    an A/B comparison. The shipped library reads no environment."""
     nvcc = _nvcc()
-    os.makedirs(BUILD_DIR, exist_ok=True)
+    build_dir = os.path.join(BUILD_DIR, "measure") if measure else BUILD_DIR
+    lib_path = os.path.join(LIB_DIR, "libhexlib_b200_measure.so") if measure else LIB_PATH
+    defines = ("HEXLIB_B200_MEASUREMENT_KNOBS",) if measure else ()
+    os.makedirs(build_dir, exist_ok=True)
     os.makedirs(LIB_DIR, exist_ok=True)
     srcs = _sources()
     with concurrent.futures.ThreadPoolExecutor(max_workers=os.cpu_count() or 4) as ex:
-        objs = list(ex.map(lambda s: _compile(nvcc, s, verbose), srcs))
-    if _stale(LIB_PATH, objs):
-        cmd = [nvcc, *ARCH_FLAGS, "-shared", "-o", LIB_PATH, *objs,
+        objs = list(ex.map(lambda s: _compile(nvcc, s, verbose, build_dir, defines), srcs))
+    if _stale(lib_path, objs):
+        cmd = [nvcc, *ARCH_FLAGS, "-shared", "-o", lib_path, *objs,
                "-cudart", "static", "-lpthread", "-ldl", "-lrt"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
-    return LIB_PATH
+    return lib_path
 
 
 if __name__ == "__main__":
-    print(build(verbose="-v" in sys.argv))
+    print(build(verbose="-v" in sys.argv, measure="--measure" in sys.argv))

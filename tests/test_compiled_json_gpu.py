@@ -63,7 +63,8 @@ def json256():
 def test_the_256_json_plan_matches_the_oracle(json256):
     ep, w, imgs, refs = json256
     out, plan = run(ep, w, imgs)
-    assert plan.n_ops == len(ep.plan.steps)
+    # the blob carries every step but the reshapes, which alias their input
+    assert plan.n_ops == sum(1 for st in ep.plan.steps if st.op.kind != "reshape")
     for i in range(2):
         assert rel_err(out[i], refs[i]) < 1e-2, f"image {i}"
 

@@ -280,10 +280,12 @@ def test_matmul_epilogue_residual():
     da, dw, db, dr = G.dev(a), G.dev(w), G.dev(bias), G.dev(r)
     G.call("hexlib_b200_matmul_epilogue_residual_fp16", G.ptr(da), G.ptr(dw), G.ptr(db),
            G.ptr(dr), G.ptr(y), M, K, N, 0, G.stream())
+    from oracle import ops
     from oracle.executor import matmul_epilogue_residual_chain
-    want = matmul_epilogue_residual_chain(a.astype(np.float32), w.astype(np.float32), bias,
-                                          r.astype(np.float32))
-    assert_close_f16(G.host(y), want, what="matmul_epilogue + residual")
+    af, wf = a.astype(np.float32), w.astype(np.float32)
+    want = matmul_epilogue_residual_chain(af, wf, bias, r.astype(np.float32))
+    product = ops.store(ops.matmul_epilogue((af, wf, bias), {"act": "none"})[0], "fp16")
+    assert_close_f16(G.host(y), want, what="matmul_epilogue + residual", inner=product)
 
 
 @pytest.mark.parametrize("Bn,M,K,N", [
