@@ -377,7 +377,12 @@ int check_op(const OpRec& op) {
       // a, w, bias, seg_cos [n, 16], seg_sin [n, 16], seg_idx [T, 2] int32, out
       HB_TRY(need(op, 7));
       HB_TRY(dt(op, 0, DT_FP16));
-      HB_TRY(dt(op, 1, DT_FP16));
+      {
+        // the weight: fp16, or q4_0 / q8_0 (blocks along N)
+        const uint32_t wdt = op.a[1].dtype;
+        if (wdt != DT_FP16 && wdt != DT_Q4_0 && wdt != DT_Q8_0) return HEXLIB_B200_ERR_REQUIRES;
+        if (wdt != DT_FP16 && op.a[1].ne[1] % 32) return HEXLIB_B200_ERR_INVAL_PARAMS;
+      }
       HB_TRY(dt(op, 2, DT_FP32));
       HB_TRY(dt(op, 3, DT_FP32));
       HB_TRY(dt(op, 4, DT_FP32));
@@ -623,6 +628,8 @@ int run_op(const OpRec& op, uint32_t n_images, int* err, void* ws, uint64_t ws_b
       g.rope_nseg = (int)a[3].ne[0];
       g.rope_T = (int)a[5].ne[0];
       g.rope_cols = op.params[1];
+      // a quantized weight arrives here already expanded (expand_weights)
+      if (a[1].dtype != DT_FP16) return HEXLIB_B200_ERR_REQUIRES;
       return hb::launch_gemm(g, err, s);
     }
     case HEXLIB_B200_KIND_LN_STATS:
@@ -830,6 +837,18 @@ struct DevBuf {
   uint32_t replicas = 1;
 };
 
+// A q4_0 / q8_0 matmul_epilogue weight of a mapped buffer and the fp16 copy
+// of it that the session's GEMMs read. `stale` until the copy has been
+// (re)computed from the current bytes of `src`.
+struct ExpandedWeight {
+  const char* src = nullptr;
+  uint64_t src_bytes = 0;
+  int qtype = 0;
+  int64_t K = 0, N = 0;
+  void* dst = nullptr;
+  bool stale = true;
+};
+
 }  // namespace
 
 struct hexlib_b200_ctx {
@@ -842,9 +861,13 @@ struct hexlib_b200_ctx {
   int* err_host = nullptr;
   int* err_dev = nullptr;
   uint64_t mapped = 0;
-  // scratch for the fp16 copy of a quantized weight, one op at a time
+  // scratch for the fp16 copy of a quantized weight, one op at a time (kept
+  // for ops that reach run_op with a quantized weight; expand_weights leaves
+  // none in a session's blobs)
   void* ws = nullptr;
   uint64_t ws_bytes = 0;
+  // the fp16 copies of the quantized GEMM weights of this session's blobs
+  std::vector<ExpandedWeight> expanded;
 };
 
 namespace {
@@ -1047,6 +1070,74 @@ static int ensure_workspace(hexlib_b200_ctx* ctx, const Parsed& p) {
   return HEXLIB_B200_OK;
 }
 
+// QUANTIZED WEIGHTS. A q4_0 / q8_0 matmul_epilogue weight is dequantized
+// ONCE per session into an fp16 copy the session keeps (one per distinct
+// weight: its address, format and shape), not once per invoke: the blob's ops
+// are rewritten to read the copy as an fp16 weight, so a quantized plan runs
+// exactly the kernels -- and, since each value is the same fp16 rounding
+// (code * d), exactly the bits -- of the fp16 plan fed the dequantized
+// weights, RoPE and residual epilogues included, with no dequantization in
+// the replayed graph. The weights of one encoder are a few hundred MB in
+// fp16, a small part of the HBM; the quantized bytes stay where the blob put
+// them and are the source of truth: a copy is recomputed (before the next
+// launch, on the session stream) whenever hexlib_b200_buf_write[_async]
+// writes any of its source bytes, and dropped with its buffer.
+static int refresh_weights(hexlib_b200_ctx* ctx) {
+  for (ExpandedWeight& e : ctx->expanded) {
+    if (!e.stale) continue;
+    const int rc = hb::launch_dequant_f16(e.qtype, e.src, e.dst, e.K, e.N, ctx->stream);
+    if (rc != HEXLIB_B200_OK) return rc;
+    e.stale = false;
+  }
+  return HEXLIB_B200_OK;
+}
+
+static int expand_weights(hexlib_b200_ctx* ctx, Parsed& p) {
+  for (OpRec& op : p.ops) {
+    if (op.kind != HEXLIB_B200_KIND_MATMUL_EPILOGUE &&
+        op.kind != HEXLIB_B200_KIND_MATMUL_EPILOGUE_RESIDUAL &&
+        op.kind != HEXLIB_B200_KIND_MATMUL_EPILOGUE_ROPE)
+      continue;
+    Arg& w = op.a[1];
+    if (w.dtype != DT_Q4_0 && w.dtype != DT_Q8_0) continue;
+    const int64_t K = w.ne[0], N = w.ne[1];
+    ExpandedWeight* hit = nullptr;
+    for (ExpandedWeight& e : ctx->expanded)
+      if (e.src == static_cast<const char*>(w.ptr) && e.qtype == (int)w.dtype && e.K == K &&
+          e.N == N)
+        hit = &e;
+    if (!hit) {
+      ExpandedWeight e;
+      e.src = static_cast<const char*>(w.ptr);
+      e.src_bytes = w.nbytes;
+      e.qtype = (int)w.dtype;
+      e.K = K;
+      e.N = N;
+      if (cudaMalloc(&e.dst, (size_t)(K * N * 2)) != cudaSuccess) {
+        cudaGetLastError();
+        return HEXLIB_B200_ERR_CUDA;
+      }
+      ctx->expanded.push_back(e);
+      hit = &ctx->expanded.back();
+    }
+    w.ptr = hit->dst;
+    w.dtype = DT_FP16;
+    w.nbytes = (uint64_t)(K * N * 2);
+  }
+  return refresh_weights(ctx);
+}
+
+// Bytes [lo, lo + n) of a mapped buffer are being rewritten.
+static void weights_written(hexlib_b200_ctx* ctx, const char* lo, uint64_t n) {
+  for (ExpandedWeight& e : ctx->expanded)
+    if (lo < e.src + e.src_bytes && e.src < lo + n) e.stale = true;
+}
+
+static void drop_expanded(hexlib_b200_ctx* ctx) {
+  for (ExpandedWeight& e : ctx->expanded) cudaFree(e.dst);
+  ctx->expanded.clear();
+}
+
 int hexlib_b200_close(hexlib_b200_ctx* ctx) {
   if (!ctx) return HEXLIB_B200_ERR_INVAL_PARAMS;
   cudaSetDevice(ctx->device);
@@ -1055,6 +1146,7 @@ int hexlib_b200_close(hexlib_b200_ctx* ctx) {
   for (auto& kv : ctx->bufs) cudaFree(kv.second.ptr);
   ctx->bufs.clear();
   if (ctx->ws) cudaFree(ctx->ws);
+  drop_expanded(ctx);
   for (cudaEvent_t e : ctx->op_events) cudaEventDestroy(e);
   if (ctx->ev0) cudaEventDestroy(ctx->ev0);
   if (ctx->ev1) cudaEventDestroy(ctx->ev1);
@@ -1109,6 +1201,7 @@ int hexlib_b200_munmap(hexlib_b200_ctx* ctx, uint32_t fd) {
   cudaSetDevice(ctx->device);
   cudaStreamSynchronize(ctx->stream);
   drop_graphs(ctx);
+  drop_expanded(ctx);     // their sources may live in this buffer
   ctx->mapped -= it->second.size * it->second.replicas;
   cudaFree(it->second.ptr);
   ctx->bufs.erase(it);
@@ -1133,6 +1226,7 @@ int hexlib_b200_buf_write(hexlib_b200_ctx* ctx, uint32_t fd, uint64_t offset,
   if (rc != HEXLIB_B200_OK) return rc;
   if (nbytes == 0) return HEXLIB_B200_OK;
   if (!src) return HEXLIB_B200_ERR_INVAL_PARAMS;
+  weights_written(ctx, p, nbytes);
   if (cudaMemcpyAsync(p, src, nbytes, cudaMemcpyHostToDevice, ctx->stream) !=
           cudaSuccess ||
       cudaStreamSynchronize(ctx->stream) != cudaSuccess) {
@@ -1165,6 +1259,7 @@ static int buf_copy_async(hexlib_b200_ctx* ctx, uint32_t fd, uint64_t offset, vo
   if (rc != HEXLIB_B200_OK) return rc;
   if (nbytes == 0) return HEXLIB_B200_OK;
   if (!host) return HEXLIB_B200_ERR_INVAL_PARAMS;
+  if (to_device) weights_written(ctx, p, nbytes);
   const cudaError_t e =
       to_device ? cudaMemcpyAsync(p, host, nbytes, cudaMemcpyHostToDevice, ctx->stream)
                 : cudaMemcpyAsync(host, p, nbytes, cudaMemcpyDeviceToHost, ctx->stream);
@@ -1283,6 +1378,11 @@ int hexlib_b200_invoke_images(hexlib_b200_ctx* ctx, const uint8_t* batch,
         write_rsp_hdr(rsp, HEXLIB_B200_ERR_TRUNCATED, 0, 0);
         return HEXLIB_B200_ERR_TRUNCATED;
       }
+      const int wrc = refresh_weights(ctx);     // copies whose source was rewritten
+      if (wrc != HEXLIB_B200_OK) {
+        write_rsp_hdr(rsp, (uint32_t)wrc, 0, 0);
+        return wrc;
+      }
       cudaEventRecord(ctx->ev0, ctx->stream);
       if (cudaGraphLaunch(g.exec, ctx->stream) != cudaSuccess) {
         cudaGetLastError();
@@ -1320,7 +1420,8 @@ int hexlib_b200_invoke_images(hexlib_b200_ctx* ctx, const uint8_t* batch,
     write_rsp_hdr(rsp, (uint32_t)rc, 0, 0);
     return rc;
   }
-  rc = ensure_workspace(ctx, p);
+  rc = expand_weights(ctx, p);
+  if (rc == HEXLIB_B200_OK) rc = ensure_workspace(ctx, p);
   if (rc != HEXLIB_B200_OK) {
     write_rsp_hdr(rsp, (uint32_t)rc, 0, 0);
     return rc;

@@ -671,8 +671,9 @@ def fuse_qkv(graph: Graph, rope_epilogue: bool = False) -> tuple[Graph, dict[str
         qkv   = rope_qk(raw, cos, sin)                       [T, 3, H, D]  (in place)
         ctx.t = attention_qkv(qkv)                           [T, H, D]
 
-    or, with `rope_epilogue` and an fp16 weight, the rotation applied by the
-    GEMM's epilogue before the one fp16 store:
+    or, with `rope_epilogue`, the rotation applied by the GEMM's epilogue
+    before the one fp16 store (a q4_0 / q8_0 weight too: the session keeps an
+    fp16 copy of it for the GEMM to read):
 
         qkv   = matmul_epilogue_rope(a, [wq|wk|wv], [bq|bk|bv],
                                      seg_cos, seg_sin, seg_idx)  [T, 3, H, D]
@@ -752,7 +753,7 @@ def fuse_qkv(graph: Graph, rope_epilogue: bool = False) -> tuple[Graph, dict[str
         for f in found:
             ed.remove(f[0], [o.outputs[0] for o in f[0]])
         ed.remove([att], att.outputs)
-        if rope_epilogue and wdt == "fp16":
+        if rope_epilogue:
             segs = []
             for i, (part, dt, shape) in enumerate((("cos", "fp32", (2 * n_tok, 16)),
                                                    ("sin", "fp32", (2 * n_tok, 16)),

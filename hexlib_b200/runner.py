@@ -154,7 +154,7 @@ SPECS: dict[str, CudaSpec] = {
         params=(Param("act", "int", ACT_CODES),),
         entry="hexlib_b200_matmul_epilogue_residual_fp16"),
     "matmul_epilogue_rope": CudaSpec(
-        "matmul_epilogue_rope", (F16, F16, F32, F32, F32, ("int32",)), "fp16",
+        "matmul_epilogue_rope", (F16, WEIGHT, F32, F32, F32, ("int32",)), "fp16",
         params=(Param("act", "int", ACT_CODES), Param("rope_cols")),
         entry="hexlib_b200_matmul_epilogue_rope_fp16"),
     "rope_qk": CudaSpec("rope_qk", (F16, F32, F32), "fp16", entry="hexlib_b200_rope_qk_fp16"),

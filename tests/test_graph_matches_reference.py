@@ -134,10 +134,15 @@ def test_rope_epilogue_rewrite_moves_the_rotation_into_the_qkv_gemm():
                 ("fp32", (512, 16)), ("fp32", (512, 16)), ("int32", (256, 2))]
             assert all(ep.derived[n][0] == "rope_segments" for n in o.inputs[3:])
     assert ep.graph.problems() == []
-    # a quantized weight keeps the separate rotation
+    # a quantized weight takes the same epilogue (the GEMM reads the session's
+    # fp16 copy of it), its packed weight staying q4_0 on the wire
     q = G.compile_for_cuda(G.build_vision_encoder(G.qwen35_at(256, weight_dtype="q4_0")),
                            residual=True, qkv=True, rope_epilogue=True)
-    assert Counter(o.kind for o in q.graph.ops)["rope_qk"] == 12
+    cq = Counter(o.kind for o in q.graph.ops)
+    assert cq["rope_qk"] == 0 and cq["matmul_epilogue_rope"] == 12
+    for o in q.graph.ops:
+        if o.kind == "matmul_epilogue_rope":
+            assert q.graph.tensors[o.inputs[1]].dtype == "q4_0"
 
 
 def test_layernorm_fold_rewrites_every_layernorm_that_feeds_a_gemm():

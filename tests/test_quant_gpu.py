@@ -162,3 +162,54 @@ def test_a_quantized_plan_gives_the_bits_of_the_fp16_plan_on_dequantized_weights
     ref = executor.run(G.compile_for_cuda(g16), dict(w16, image=imgs[0]))["merger.out"]
     rel = np.abs(outs[1][0].astype(np.float64) - ref).max() / np.abs(ref).max()
     assert rel < 1e-2, rel
+
+
+def _dequantized_feeds(gq, wq, dtype):
+    w16 = dict(wq)
+    for n, t in gq.tensors.items():
+        if t.const and t.dtype == dtype:
+            w16[n] = oq.dequantize_f16(quant.quantize(wq[n], dtype), t.shape, dtype)
+    return w16
+
+
+@pytest.mark.parametrize("dtype", ["q4_0", "q8_0"])
+def test_a_quantized_plan_with_every_default_rewrite_gives_the_fp16_plans_bits(enc256, dtype):
+    """With the RoPE and residual epilogues and the packed q/k/v GEMM, the
+    quantized plan's GEMMs read the session's fp16 copies of the weights: the
+    same kernels, the same bits as the fp16 plan fed the dequantized weights."""
+    cfg_q = G.qwen35_at(256, weight_dtype=dtype)
+    gq = G.build_vision_encoder(cfg_q)
+    wq = F.weights(cfg_q, 0, gq)
+    g16 = G.build_vision_encoder(enc256)
+    imgs = F.images(enc256, 2, 4)
+    outs = []
+    for g, w in ((gq, wq), (g16, _dequantized_feeds(gq, wq, dtype))):
+        plan = wholeplan.build_cuda_plan(G.compile_for_cuda(g, **G.DEFAULT_REWRITES), w,
+                                         alias=True)
+        with Session(0) as s:
+            s.load(plan, max_images=2)
+            outs.append(s.run(np.ascontiguousarray(imgs)))
+    assert "matmul_epilogue_rope" in plan.kinds
+    np.testing.assert_array_equal(outs[0], outs[1])
+
+
+def test_rewriting_a_quantized_weight_refreshes_the_sessions_copy(enc256):
+    """The quantized bytes are the source of truth: new consts written into
+    the mapped buffer are seen by the next replay of the cached graph."""
+    cfg_q = G.qwen35_at(256, weight_dtype="q4_0")
+    gq = G.build_vision_encoder(cfg_q)
+    ep = G.compile_for_cuda(gq, **G.DEFAULT_REWRITES)
+    p1 = wholeplan.build_cuda_plan(ep, F.weights(cfg_q, 0, gq), alias=True)
+    p2 = wholeplan.build_cuda_plan(ep, F.weights(cfg_q, 5, gq), alias=True)
+    assert p1.blob == p2.blob and p1.const_payload != p2.const_payload
+    imgs = np.ascontiguousarray(F.images(enc256, 1, 6))
+    with Session(0) as s:
+        s.load(p1, max_images=1)
+        out1 = s.run(imgs)
+        s.write(wholeplan.CONST_FD, 0, np.frombuffer(p2.const_payload, np.uint8))
+        out2 = s.run(imgs)                                         # cached graph replay
+    with Session(0) as s:
+        s.load(p2, max_images=1)
+        want2 = s.run(imgs)
+    assert not np.array_equal(out1, out2)
+    np.testing.assert_array_equal(out2, want2)
