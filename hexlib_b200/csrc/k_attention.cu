@@ -80,7 +80,6 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
   return d;
 }
 
-template <bool HALF_EXP>
 __global__ void __launch_bounds__(AT_THREADS, 1)
     attention_tc(const __grid_constant__ CUtensorMap tmQ,
                  const __grid_constant__ CUtensorMap tmK,
@@ -247,9 +246,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     const uint32_t o_col = tmem + lane_off + 256u + (uint32_t)(t * AT_D);
     const uint32_t p_col = tmem + lane_off + 384u + (uint32_t)(t * 64);
     const float c = p.c_log2;
-    // (2^8 margin with fp32 exponentials; with fp16 arguments 2^1, so the
-    // largest terms keep the argument's fp16 precision at its finest)
-    constexpr float kRescale = HALF_EXP ? 1.0f : 8.0f;
+    constexpr float kRescale = 8.0f;
     uint32_t g0 = 0;
     int64_t i = 0;
     for (int64_t w = blockIdx.x; w < items; w += gridDim.x, ++i, g0 += nkv) {
@@ -307,8 +304,6 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         // row's lane of P in TMEM (column e holds keys 2e and 2e + 1).
         // (pairs of keys through sm_100's two-wide FMA and add: the same
         // roundings as two scalar operations, half the instructions)
-        // HALF_EXP: the pair's argument rounded to fp16 and exponentiated by one
-        // packed fp16 ex2, the row sum taken over the rounded P it stores.
         const float2 c2 = make_float2(c, c), nm2 = make_float2(-m_use, -m_use);
         float2 ps[4];
 #pragma unroll
@@ -321,19 +316,11 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             const int x = k32 * 32 + 2 * e;
             const float2 a = __ffma2_rn(make_float2(__uint_as_float(sv[x]),
                                                     __uint_as_float(sv[x + 1])), c2, nm2);
-            if constexpr (HALF_EXP) {
-              uint32_t hp;
-              asm("ex2.approx.f16x2 %0, %1;" : "=r"(hp) : "r"(pack_half2(a.x, a.y)));
-              const float2 pf = __half22float2(*reinterpret_cast<const __half2*>(&hp));
-              ps[e & 3] = __fadd2_rn(ps[e & 3], pf);
-              h2[e] = hp;
-            } else {
-              const float p0 = ex2_approx(a.x);
-              const float p1 = ex2_approx(a.y);
-              ps[e & 3].x += p0;
-              ps[e & 3].y += p1;
-              h2[e] = pack_half2(p0, p1);
-            }
+            const float p0 = ex2_approx(a.x);
+            const float p1 = ex2_approx(a.y);
+            ps[e & 3].x += p0;
+            ps[e & 3].y += p1;
+            h2[e] = pack_half2(p0, p1);
           }
           tmem_st_32x32b_x16(p_col + (uint32_t)(k32 * 16), h2);
         }
@@ -436,18 +423,10 @@ bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u
 
 int g_sms = 0;
 
-// The exponential variant: fp32 (one MUFU.EX2 per score) unless built with
-// HEXLIB_B200_ATTN_HALF_EXP (for comparisons).
-#ifdef HEXLIB_B200_ATTN_HALF_EXP
-constexpr bool kHalfExp = true;
-#else
-constexpr bool kHalfExp = false;
-#endif
-
 }  // namespace
 
 int attention_kernels_init() {
-  if (cudaFuncSetAttribute(attention_tc<kHalfExp>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  if (cudaFuncSetAttribute(attention_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            AT_SMEM) != cudaSuccess) {
     cudaGetLastError();
     return HEXLIB_B200_ERR_CUDA;
@@ -495,7 +474,7 @@ int launch_attention(const void* q, const void* k, const void* v, void* ctx, int
       p.out = reinterpret_cast<__half*>(ctx);
       p.err = err;
       p.reverse = order_next();
-      attention_tc<kHalfExp><<<persistent_grid(Bn * p.q_pairs), AT_THREADS, AT_SMEM, s>>>(mq, mk, mv, p);
+      attention_tc<<<persistent_grid(Bn * p.q_pairs), AT_THREADS, AT_SMEM, s>>>(mq, mk, mv, p);
       if (cudaPeekAtLastError() != cudaSuccess) {
         cudaGetLastError();
         return HEXLIB_B200_ERR_CUDA;
@@ -543,7 +522,7 @@ int launch_attention_qkv(const void* qkv, void* ctx, int64_t B, int T, int H, in
   p.out = reinterpret_cast<__half*>(ctx);
   p.err = err;
   p.reverse = order_next();
-  attention_tc<kHalfExp><<<persistent_grid(p.Bn * p.q_pairs), AT_THREADS, AT_SMEM, s>>>(m, m, m, p);
+  attention_tc<<<persistent_grid(p.Bn * p.q_pairs), AT_THREADS, AT_SMEM, s>>>(m, m, m, p);
   if (cudaPeekAtLastError() != cudaSuccess) {
     cudaGetLastError();
     return HEXLIB_B200_ERR_CUDA;
