@@ -183,10 +183,13 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         const int qb = (int)(i & 1);
         if (!mbar_wait(&q_full[qb], (uint32_t)(i >> 1) & 1u, abort_flag, p.err)) goto done;
         // S_t(j) = Q_t K_j^T, once the softmax has read S_t(j-1) out of TMEM
+        // (and K_j, V_j have landed: waited for by the first tile's S(j),
+        // which the second tile's S(j) always follows directly)
         auto issue_s = [&](int t, int j) -> bool {
           const uint32_t g = g0 + (uint32_t)j;
           const int st = (int)(g % AT_STAGES);
-          if (!mbar_wait(&kv_full[st], (g / AT_STAGES) & 1u, abort_flag, p.err)) return false;
+          if (t == 0 && !mbar_wait(&kv_full[st], (g / AT_STAGES) & 1u, abort_flag, p.err))
+            return false;
           if (g > 0 && !mbar_wait(&s_free[t], (g - 1) & 1u, abort_flag, p.err)) return false;
           tc_fence_after();
           const uint32_t qa = smem_u32(sQ + (qb * 2 + t) * AT_TILE);
@@ -220,11 +223,13 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         };
         if (!issue_s(0, 0) || !issue_s(1, 0)) goto done;
         for (int j = 0; j < nkv; ++j) {
-          // S(j+1) goes in ahead of P(j)V(j), so a tile's next scores are
-          // ready by the time its softmax finishes the current block.
+          // Both tiles' S(j+1) go in ahead of their P(j)V(j): each tile's
+          // next scores are ready by the time its softmax finishes the
+          // current block, and neither tile's scores wait behind the other
+          // tile's P V, so the two tiles' softmax phases overlap.
           if (j + 1 < nkv && !issue_s(0, j + 1)) goto done;
-          if (!issue_pv(0, j)) goto done;
           if (j + 1 < nkv && !issue_s(1, j + 1)) goto done;
+          if (!issue_pv(0, j)) goto done;
           if (!issue_pv(1, j)) goto done;
           umma_commit(&kv_empty[(g0 + (uint32_t)j) % AT_STAGES]);   // K_j, V_j consumed
         }
