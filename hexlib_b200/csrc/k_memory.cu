@@ -396,6 +396,65 @@ __global__ void __launch_bounds__(kThreads) layernorm_rows(const uint4* __restri
   }
 }
 
+// layernorm with one row per warp (32 lanes x V vectors) and the affine
+// weight and bias in registers: a lane meets the same V * 8 columns in every
+// row it walks, so it loads their weight and bias once per launch instead of
+// four 16-byte loads per 8 outputs per row, which for fp32 weights is four
+// times the row's own bytes in L1 traffic. D rows of each warp are in flight
+// ahead of the one being reduced (D = 1 and 2 measured alike in the encoder).
+#ifndef HB_LN_DEPTH
+#define HB_LN_DEPTH 1
+#endif
+template <int V, int D>
+__global__ void __launch_bounds__(kThreads) layernorm_rows_wb(const uint4* __restrict__ x,
+                                                              const float* __restrict__ w,
+                                                              const float* __restrict__ b,
+                                                              uint4* __restrict__ y, int64_t R,
+                                                              float eps, int rev) {
+  constexpr int G = 32;
+  __shared__ float red[kThreads / 32];
+  const RowWalk<G> rw;
+  auto at = [&](int64_t k) { return rev ? R - 1 - k : k; };
+  float ww[V][8], bb[V][8];
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    const int c0 = (j * G + rw.g) * 8;
+    const float4 w0 = __ldg(reinterpret_cast<const float4*>(w + c0));
+    const float4 w1 = __ldg(reinterpret_cast<const float4*>(w + c0 + 4));
+    const float4 b0 = __ldg(reinterpret_cast<const float4*>(b + c0));
+    const float4 b1 = __ldg(reinterpret_cast<const float4*>(b + c0 + 4));
+    ww[j][0] = w0.x; ww[j][1] = w0.y; ww[j][2] = w0.z; ww[j][3] = w0.w;
+    ww[j][4] = w1.x; ww[j][5] = w1.y; ww[j][6] = w1.z; ww[j][7] = w1.w;
+    bb[j][0] = b0.x; bb[j][1] = b0.y; bb[j][2] = b0.z; bb[j][3] = b0.w;
+    bb[j][4] = b1.x; bb[j][5] = b1.y; bb[j][6] = b1.z; bb[j][7] = b1.w;
+  }
+  uint4 nxt[D][V];
+#pragma unroll
+  for (int d = 0; d < D; ++d)
+    if (rw.first + d * rw.step < R) row_load<G, V>(nxt[d], x, at(rw.first + d * rw.step), rw.g);
+  for (int64_t r = rw.first; r < R; r += rw.step) {
+    float v[V][8];
+    unpack_rows<V>(v, nxt[0]);
+#pragma unroll
+    for (int d = 0; d + 1 < D; ++d)
+#pragma unroll
+      for (int j = 0; j < V; ++j) nxt[d][j] = nxt[d + 1][j];
+    if (r + D * rw.step < R) row_load<G, V>(nxt[D - 1], x, at(r + D * rw.step), rw.g);
+    float mean, inv;
+    row_moments<G, V>(v, red, eps, mean, inv);
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      H8 o;
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        o.h2[q] = __floats2half2_rn((v[j][2 * q] - mean) * inv * ww[j][2 * q] + bb[j][2 * q],
+                                    (v[j][2 * q + 1] - mean) * inv * ww[j][2 * q + 1] +
+                                        bb[j][2 * q + 1]);
+      y[at(r) * (G * V) + j * G + rw.g] = o.u;
+    }
+  }
+}
+
 // The row statistics of layernorm alone: (mean, 1/sqrt(var + eps)) per row,
 // computed exactly as layernorm_rows computes them, for a GEMM that applies
 // the normalisation in its epilogue (the affine weight folded into its
@@ -1033,9 +1092,10 @@ int memory_kernels_init() {
 #define HB_NOTE_ROWS(K)                                                             \
   note((const void*)K<8, 1>); note((const void*)K<16, 1>); note((const void*)K<32, 1>); \
   note((const void*)K<32, 2>); note((const void*)K<32, 3>); note((const void*)K<32, 4>); \
-  note((const void*)K<16, 6>);                                                              \
   note((const void*)K<256, 1>); note((const void*)K<256, 2>); note((const void*)K<256, 4>);
   HB_NOTE_ROWS(layernorm_rows)
+  note((const void*)layernorm_rows_wb<2, HB_LN_DEPTH>);
+  note((const void*)layernorm_rows_wb<3, HB_LN_DEPTH>);
   HB_NOTE_ROWS(ln_stats_rows)
   HB_NOTE_ROWS(rmsnorm_rows)
   HB_NOTE_ROWS(softmax_rows)
@@ -1172,7 +1232,6 @@ int launch_rows(F* kern, int g, int64_t R, cudaStream_t s, A... args) {
     case 32 * 16 + 2: return launch_rows(K<32, 2>, 32, R, s, __VA_ARGS__);         \
     case 32 * 16 + 3: return launch_rows(K<32, 3>, 32, R, s, __VA_ARGS__);         \
     case 32 * 16 + 4: return launch_rows(K<32, 4>, 32, R, s, __VA_ARGS__);         \
-    case 16 * 16 + 6: return launch_rows(K<16, 6>, 16, R, s, __VA_ARGS__);         \
     case 256 * 16 + 1: return launch_rows(K<256, 1>, 256, R, s, __VA_ARGS__);      \
     case 256 * 16 + 2: return launch_rows(K<256, 2>, 256, R, s, __VA_ARGS__);      \
     case 256 * 16 + 4: return launch_rows(K<256, 4>, 256, R, s, __VA_ARGS__);      \
@@ -1184,9 +1243,17 @@ int launch_layernorm_f16(const void* x, const float* w, const float* b,
   if (R == 0) return HEXLIB_B200_OK;
   const bool al = aligned16(x) && aligned16(y) && aligned16(w) && aligned16(b);
   RowCfg cfg = al ? row_cfg(C) : RowCfg{0, 0};
-  // C = 768: two rows per warp, 16 lanes x 6 vectors each, so one chain of
-  // shuffles reduces both rows
-  if (cfg.g == 32 && cfg.v == 3) cfg = RowCfg{16, 6};
+  // rows of 512 and 768: one row per warp, weight and bias in registers
+  // (at 512^2 x 64 in the encoder 48.5 -> 41.7 us against two rows per warp
+  // of 16 lanes x 6 vectors that load them per row)
+  if (cfg.g == 32 && (cfg.v == 2 || cfg.v == 3)) {
+    switch (cfg.v) {
+      case 2: return launch_rows(layernorm_rows_wb<2, HB_LN_DEPTH>, 32, R, s, (const uint4*)x,
+                                 w, b, (uint4*)y, R, eps, order_next());
+      case 3: return launch_rows(layernorm_rows_wb<3, HB_LN_DEPTH>, 32, R, s, (const uint4*)x,
+                                 w, b, (uint4*)y, R, eps, order_next());
+    }
+  }
   HB_ROW_SWITCH(layernorm_rows, cfg, R, s, (const uint4*)x, w, b, (uint4*)y, R, eps,
                 order_next())
   layernorm_f16_generic<<<grid_for(R * 32, kThreads), kThreads, 0, s>>>(
