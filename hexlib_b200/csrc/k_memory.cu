@@ -327,8 +327,9 @@ __device__ __forceinline__ float frag_max(const float (&v)[V][8]) {
 
 // A row's mean and 1/sqrt(biased variance + eps), the variance taken over
 // the centred values (two passes over the row in registers). Shared by
-// layernorm_rows and ln_stats_rows, so the statistics a folded-layernorm GEMM
-// applies are exactly the ones layernorm_rows uses. (Running sums in one
+// layernorm_rows, layernorm_rows_wb and ln_stats_rows, which lay a row out the
+// same way for a given width, so the statistics a folded-layernorm GEMM
+// applies are exactly the ones the unfolded layernorm uses. (Running sums in one
 // chain: with four chains and two-wide arithmetic the 768-wide variant
 // needs 130 registers, halving its residency, and measured 7-9% slower.)
 template <int G, int V>
