@@ -130,6 +130,12 @@ class EmbeddingGather:
         if out.numel() != local.numel() * self.world or not (local.is_contiguous()
                                                              and out.is_contiguous()):
             raise ValueError("out must hold world x local, both contiguous")
+        # NCCL's kernel runs on the communicator's device and would otherwise
+        # be handed another device's memory
+        for t in (local, out):
+            if t.device.type != "cuda" or t.device.index != self.device:
+                raise ValueError(f"the gather's tensors must be on cuda:{self.device}, "
+                                 f"not {t.device}")
         rc = self._L.hexlib_b200_nccl_allgather_f16(self._h, local.data_ptr(), out.data_ptr(),
                                                     local.numel(), stream, self.timeout_ms)
         if rc != 1:

@@ -392,7 +392,10 @@ HEXLIB_B200_API int hexlib_b200_nccl_available(void);
 /* Rank 0's rendezvous id (128 bytes), to be shared with every rank. */
 HEXLIB_B200_API int hexlib_b200_nccl_unique_id(uint8_t *id_out);
 /* Join the communicator `id` as `rank` of `nranks` on CUDA device `device`,
- * non-blocking, waiting at most timeout_ms for every rank to join. */
+ * non-blocking, waiting at most timeout_ms for every rank to join. This and
+ * the calls below on the communicator make `device` the calling thread's
+ * current CUDA device and leave it so (one process per GPU is the use they
+ * serve, where it already is). */
 HEXLIB_B200_API int hexlib_b200_nccl_open(const uint8_t *id, int nranks, int rank,
                                           int device, uint32_t timeout_ms,
                                           hexlib_b200_comm **out);

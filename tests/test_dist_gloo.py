@@ -152,3 +152,20 @@ def test_the_nccl_entries_refuse_bad_arguments_without_a_device():
     assert L.hexlib_b200_nccl_wait(None, None, 100) == wire.STATUS["ERR_NOT_STARTED"]
     assert L.hexlib_b200_nccl_unique_id(None) == wire.STATUS["ERR_INVAL_PARAMS"]
     assert L.hexlib_b200_nccl_close(None, 0) == wire.STATUS["OK"]
+
+
+def test_the_gather_refuses_tensors_off_its_device_before_calling_nccl():
+    import pytest
+    import torch
+
+    from hexlib_b200 import dist as D
+    g = object.__new__(D.EmbeddingGather)     # no communicator: the checks come first
+    g.rank, g.world, g.device, g.timeout_ms, g._h = 0, 2, 0, 100, None
+    local = torch.zeros((2, 4), dtype=torch.float16)
+    out = torch.zeros((4, 4), dtype=torch.float16)
+    with pytest.raises(ValueError, match="cuda:0"):
+        g.gather(local, out, 0)
+    with pytest.raises(TypeError):
+        g.gather(local.float(), out, 0)
+    with pytest.raises(ValueError, match="world x local"):
+        g.gather(local, out[:3], 0)
